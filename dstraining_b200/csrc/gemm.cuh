@@ -1,0 +1,373 @@
+// Persistent warp-specialised bf16 GEMM on the sm_100a tensor cores.
+//
+//   C[M, N] = A[M, K] . B[N, K]^T   (fp32 accumulate in TMEM, fused epilogue)
+//
+// A and B are each either K-major ("row-major [rows][K]") or MN-major
+// ("[K][rows]"), which covers every product a linear layer needs:
+//   forward  y  = x W^T : A = x  (K-major), B = W  (K-major)
+//   backward dx = dy W  : A = dy (K-major), B = W  (MN-major)
+//   backward dW = dy^T x: A = dy (MN-major), B = x (MN-major)
+//
+// Structure (one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer: 128B-swizzled tiles of A and B into a ring of
+//               smem stages, completion on per-stage "full" mbarriers.
+//   warp 1      TMEM allocator + MMA issuer: one elected thread issues
+//               tcgen05.mma (M=128, N=BN, K=16) x 4 per 64-wide K stage and
+//               tcgen05.commit's the stage back to the producer; after a
+//               tile's last stage it commits the accumulator to the epilogue.
+//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time (one TMEM lane =
+//               one output row per thread), apply the fused epilogue, store.
+// The accumulator is double-buffered in TMEM (2 x BN fp32 columns), so the
+// epilogue of tile i overlaps the MMAs of tile i+1.
+//
+// Split-K: a work unit is (tile, k-split). With splits > 1 the epilogue
+// writes fp32 partial tiles to a workspace and a separate kernel sums them in
+// split order (deterministic, no atomics).
+#pragma once
+
+#include "ptx.cuh"
+
+namespace dst {
+
+enum Epilogue : int {
+  kEpiStore = 0,      // C = acc
+  kEpiBias = 1,       // C = acc + bias[n]
+  kEpiBiasGelu = 2,   // aux_out = acc + bias (pre-activation), C = gelu(aux_out)
+  kEpiBiasResid = 3,  // C = acc + bias[n] + aux[m, n]
+  kEpiDGelu = 4,      // C = acc * gelu'(aux[m, n])
+  kEpiPartialF32 = 5, // ws[split][m][n] = acc (fp32)
+  kEpiCEStats = 6,    // C = bf16(acc); per (row, tile): max / sum exp; target logit
+  kEpiAccumF32 = 7,   // accf32[m, n] += acc  (fp32 output, e.g. grad accumulation)
+};
+
+struct GemmParams {
+  int M, N, K;
+  int splits;             // K splits (>= 1)
+  int k_blocks_per_split; // in units of 64
+  __nv_bfloat16* out;     // [M, ldo]
+  int ldo;
+  const __nv_bfloat16* bias;  // [N] or null
+  const __nv_bfloat16* aux;   // [M, ld_aux] (residual / pre-activation)
+  int ld_aux;
+  __nv_bfloat16* aux_out;     // [M, ldo] (pre-activation output)
+  float* ws;                  // split-K workspace [splits, M, N] / fp32 accumulation target [M, N]
+  // CE statistics epilogue
+  float* ce_max;        // [M, n_tiles]
+  float* ce_sum;        // [M, n_tiles]
+  float* ce_tgt;        // [M]
+  const int64_t* ce_targets;  // [M]
+  int ce_col0;          // global vocab id of local column 0
+  int ce_valid_cols;    // local columns < this are real vocab entries
+  int* status;
+};
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kGemmThreads = 192;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int kStageA = kBM * kBK * 2;
+  static constexpr int kStageB = BN * kBK * 2;
+  static constexpr int kStageBytes = kStageA + kStageB;
+  static constexpr int kStages = (BN == 256) ? 4 : 6;
+  static constexpr int kTmemCols = 2 * BN;  // power of two: 256 or 512
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&v)[32], int valid) {
+  // valid: number of columns (multiple of 8) that are inside N.
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    if (q * 8 < valid) {
+      uint4 pk;
+      uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(v[q * 8 + 2 * j], v[q * 8 + 2 * j + 1]);
+        w[j] = *reinterpret_cast<uint32_t*>(&h);
+      }
+      *reinterpret_cast<uint4*>(dst + q * 8) = pk;
+    }
+  }
+}
+
+__device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float (&v)[32], int valid) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    if (q * 8 < valid) {
+      uint4 pk = *reinterpret_cast<const uint4*>(src + q * 8);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&pk);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 f = __bfloat1622float2(h[j]);
+        v[q * 8 + 2 * j] = f.x;
+        v[q * 8 + 2 * j + 1] = f.y;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[q * 8 + j] = 0.f;
+    }
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte alignment for the 128B swizzle atoms.
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stage_base = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* full_bar = bars;               // [S]
+  uint64_t* empty_bar = bars + S;          // [S]
+  uint64_t* tfull_bar = bars + 2 * S;      // [2]
+  uint64_t* tempty_bar = bars + 2 * S + 2; // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  const int num_m = (p.M + kBM - 1) / kBM;
+  const int num_n = (p.N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_units = num_tiles * p.splits;
+  const int k_blocks_total = (p.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull_bar[i], 1);
+      mbar_init(&tempty_bar[i], 128);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+        const int tile = u % num_tiles;
+        const int split = u / num_tiles;
+        const int m0 = (tile % num_m) * kBM;
+        const int n0 = (tile / num_m) * BN;
+        const int kb0 = split * p.k_blocks_per_split;
+        const int kb1 = min(kb0 + p.k_blocks_per_split, k_blocks_total);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, p.status, kTimeoutSmemEmpty)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = stage_base + stage * Cfg::kStageBytes;
+          uint8_t* sb = sa + Cfg::kStageA;
+          mbar_arrive_expect_tx(&full_bar[stage], Cfg::kStageBytes);
+          const int k0 = kb * kBK;
+          if (!A_MN) {
+            tma_load_2d(sa, &tmA, &full_bar[stage], k0, m0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < kBM / 64; ++j) tma_load_2d(sa + j * 64 * kBK * 2, &tmA, &full_bar[stage], m0 + 64 * j, k0);
+          }
+          if (!B_MN) {
+            tma_load_2d(sb, &tmB, &full_bar[stage], k0, n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + j * 64 * kBK * 2, &tmB, &full_bar[stage], n0 + 64 * j, k0);
+          }
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc = idesc_bf16_f32(kBM, BN, A_MN, B_MN);
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int iter = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++iter) {
+        const int split = u / num_tiles;
+        const int kb0 = split * p.k_blocks_per_split;
+        const int kb1 = min(kb0 + p.k_blocks_per_split, k_blocks_total);
+        const int acc = iter & 1;
+        const uint32_t acc_phase = (iter >> 1) & 1;
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, p.status, kTimeoutTmemEmpty)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, p.status, kTimeoutTmaFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(stage_base + stage * Cfg::kStageBytes);
+          const uint32_t sb = sa + Cfg::kStageA;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            uint64_t da, db;
+            if (!A_MN)
+              da = smem_desc_sw128(sa + kk * 32, 16, 1024);
+            else
+              da = smem_desc_sw128(sa + kk * 2048, 64 * kBK * 2, 1024);
+            if (!B_MN)
+              db = smem_desc_sw128(sb + kk * 32, 16, 1024);
+            else
+              db = smem_desc_sw128(sb + kk * 2048, 64 * kBK * 2, 1024);
+            umma_f16_ss(d_tmem, da, db, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty_bar[stage]);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (kb1 <= kb0) {
+          // Empty K range (cannot happen for valid shapes): still hand the
+          // (zero) accumulator over so the epilogue does not wait forever.
+        }
+        umma_commit(&tfull_bar[acc]);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row_in_tile = quad * 32 + lane;
+    int iter = 0;
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++iter) {
+      const int tile = u % num_tiles;
+      const int split = u / num_tiles;
+      const int m_blk = tile % num_m;
+      const int n_blk = tile / num_m;
+      const int m0 = m_blk * kBM;
+      const int n0 = n_blk * BN;
+      const int acc = iter & 1;
+      const uint32_t acc_phase = (iter >> 1) & 1;
+      if (!mbar_wait(&tfull_bar[acc], acc_phase, p.status, kTimeoutTmemFull)) break;
+      tc_fence_after();
+      const int row = m0 + row_in_tile;
+      const bool row_ok = row < p.M;
+      float ce_m = -INFINITY, ce_s = 0.f;
+      int64_t tgt = -1;
+      if (EPI == kEpiCEStats && row_ok) tgt = p.ce_targets[row] - p.ce_col0;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        tmem_ld32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN + c * 32, v);
+        tmem_wait_ld();
+        const int col = n0 + c * 32;
+        if (!row_ok || col >= p.N) continue;
+        const int valid = min(32, p.N - col);
+        if (EPI == kEpiPartialF32) {
+          float* dst = p.ws + (static_cast<size_t>(split) * p.M + row) * p.N + col;
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            if (q * 4 < valid) *reinterpret_cast<float4*>(dst + q * 4) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+          continue;
+        }
+        if (EPI == kEpiAccumF32) {
+          float* dst = p.ws + static_cast<size_t>(row) * p.N + col;
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            if (q * 4 < valid) {
+              float4 o = *reinterpret_cast<float4*>(dst + q * 4);
+              o.x += v[4 * q];
+              o.y += v[4 * q + 1];
+              o.z += v[4 * q + 2];
+              o.w += v[4 * q + 3];
+              *reinterpret_cast<float4*>(dst + q * 4) = o;
+            }
+          continue;
+        }
+        if (EPI == kEpiBias || EPI == kEpiBiasGelu || EPI == kEpiBiasResid) {
+          if (p.bias != nullptr) {
+            float b[32];
+            load_bf16x32(p.bias + col, b, valid);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] += b[i];
+          }
+        }
+        __nv_bfloat16* out = p.out + static_cast<size_t>(row) * p.ldo + col;
+        if (EPI == kEpiBiasGelu) {
+          store_bf16x32(p.aux_out + static_cast<size_t>(row) * p.ldo + col, v, valid);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            // gelu of the bf16-rounded pre-activation, so forward and the
+            // dGELU backward see the same input.
+            float x = __bfloat162float(__float2bfloat16_rn(v[i]));
+            v[i] = gelu_tanh(x);
+          }
+        } else if (EPI == kEpiBiasResid) {
+          float r[32];
+          load_bf16x32(p.aux + static_cast<size_t>(row) * p.ld_aux + col, r, valid);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] += r[i];
+        } else if (EPI == kEpiDGelu) {
+          float x[32];
+          load_bf16x32(p.aux + static_cast<size_t>(row) * p.ld_aux + col, x, valid);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] *= gelu_tanh_grad(x[i]);
+        } else if (EPI == kEpiCEStats) {
+          float cm = -INFINITY;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            v[i] = __bfloat162float(__float2bfloat16_rn(v[i]));
+            const int lc = col + i;  // local column
+            if (lc < p.ce_valid_cols) cm = fmaxf(cm, v[i]);
+            if (lc == tgt) p.ce_tgt[row] = v[i];
+          }
+          if (cm > -INFINITY) {
+            const float nm = fmaxf(ce_m, cm);
+            float s = 0.f;
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (col + i < p.ce_valid_cols) s += __expf(v[i] - nm);
+            ce_s = ce_s * __expf(ce_m - nm) + s;
+            ce_m = nm;
+          }
+        }
+        store_bf16x32(out, v, valid);
+      }
+      if (EPI == kEpiCEStats && row_ok) {
+        const int n_tiles = num_n;
+        p.ce_max[static_cast<size_t>(row) * n_tiles + n_blk] = ce_m;
+        p.ce_sum[static_cast<size_t>(row) * n_tiles + n_blk] = ce_s;
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty_bar[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+}  // namespace dst

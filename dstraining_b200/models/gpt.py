@@ -118,6 +118,10 @@ class MLP(nn.Module):
         )
 
     def forward(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if native.active(x, self.c_fc.weight):
+            from ..ops.linear import mlp
+
+            return mlp(x, self.c_fc, self.c_proj, residual)
         return self.c_proj(self.c_fc(x, activation="gelu_tanh"), residual=residual)
 
 

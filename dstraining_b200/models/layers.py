@@ -81,10 +81,11 @@ class ColumnParallelLinear(nn.Module):
 
     def forward(self, x: torch.Tensor, activation: Optional[str] = None) -> torch.Tensor:
         assert activation in ACTIVATIONS
-        if native.active(x, self.weight) and not self.gather_output:
+        if native.active(x, self.weight):
             from ..ops.linear import column_parallel_linear
 
-            return column_parallel_linear(x, self.weight, self.bias, self.tp, self.input_mode, activation)
+            y = column_parallel_linear(x, self.weight, self.bias, self.tp, self.input_mode, activation)
+            return gather_from_tp_region(y, self.tp) if self.gather_output else y
         if self.input_mode == "sequence":
             x = gather_along_seq(x, self.tp)
         else:

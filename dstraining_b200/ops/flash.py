@@ -1,0 +1,29 @@
+"""Autograd wrapper of the native causal flash attention (``csrc/attn.cu``)."""
+
+from __future__ import annotations
+
+import torch
+
+from . import native
+
+
+class _FlashFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qkv, n_head, head_dim):
+        qkv = qkv.contiguous()
+        out, lse = native.lib().flash_attn_fwd(qkv, n_head, head_dim)
+        ctx.save_for_backward(qkv, out, lse)
+        ctx.meta = (n_head, head_dim)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        qkv, out, lse = ctx.saved_tensors
+        n_head, head_dim = ctx.meta
+        dqkv = native.lib().flash_attn_bwd(dout.contiguous(), qkv, out, lse, n_head, head_dim)
+        return dqkv, None, None
+
+
+def flash_attention(qkv: torch.Tensor, n_head: int, head_dim: int) -> torch.Tensor:
+    """qkv [B, T, n_head * 3 * head_dim] (head-major q|k|v) -> [B, T, n_head * head_dim]."""
+    return _FlashFn.apply(qkv, n_head, head_dim)

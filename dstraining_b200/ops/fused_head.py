@@ -1,0 +1,63 @@
+"""Fused LM head + (vocab-parallel) cross-entropy on the native path.
+
+Forward runs the head GEMM with a softmax-statistics epilogue: each output
+tile reduces its fp32 accumulator rows to (max, sum exp) and picks the target
+logit when the target id falls inside the tile, so the loss needs no pass
+over the logits. Per-tile stats merge in tile order into per-row stats; under
+TP the ``[3, N]`` per-rank stats are all-gathered and merged in rank order
+(one collective; bitwise identical on every rank).
+
+Backward turns the saved bf16 logits into ``(softmax - onehot) * grad / N`` in
+place and runs the two backward GEMMs (dX = dlogits W, dW = dlogits^T X) on
+them. Same math as :mod:`dstraining_b200.ops.cross_entropy`.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from ..ops import native
+from ..parallel.comm import all_gather_dim, all_reduce_sum, reduce_scatter_dim
+from ..parallel.topology import TPContext
+from .cross_entropy import merge_stats
+from .gemm import EPI_STORE, gemm
+
+
+class _FusedHeadCE(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, targets, tp, real_vocab, seq_parallel):
+        lib = native.lib()
+        if seq_parallel and tp.enabled:
+            x = all_gather_dim(x, tp, 1)
+        x2 = x.reshape(-1, x.shape[-1]).contiguous()
+        tg = targets.reshape(-1).contiguous()
+        v_local = w.shape[0]
+        col0 = tp.rank * v_local
+        valid = max(0, min(v_local, real_vocab - col0))
+        logits, tmax, tsum, tgt = lib.gemm_ce_stats(x2, w, tg, col0, valid)
+        m, s = lib.ce_merge_tiles(tmax, tsum)
+        stats = torch.stack([m, s, tgt])[None]
+        if tp.enabled:
+            stats = all_gather_dim(stats, tp, 0)
+        lse, tgt_all = merge_stats(stats)
+        loss = (lse - tgt_all).mean()
+        ctx.save_for_backward(logits, lse, x2, w, tg)
+        ctx.meta = (tp, seq_parallel, col0, valid, x.shape)
+        return loss
+
+    @staticmethod
+    def backward(ctx, g):
+        logits, lse, x2, w, tg = ctx.saved_tensors
+        tp, seq_parallel, col0, valid, xshape = ctx.meta
+        lib = native.lib()
+        n = logits.shape[0]
+        lib.ce_grad_inplace(logits, lse.contiguous(), tg, col0, valid, g.float().reshape(1).contiguous(), 1.0 / n)
+        dx = gemm(logits, False, w, True, EPI_STORE).view(xshape)
+        dw = gemm(logits, True, x2, True, EPI_STORE)
+        if tp.enabled:
+            dx = reduce_scatter_dim(dx, tp, 1) if seq_parallel else all_reduce_sum(dx, tp)
+        return dx, dw, None, None, None, None
+
+
+def fused_head_loss(x, w, targets, tp: TPContext, real_vocab: int, seq_parallel: bool):
+    return _FusedHeadCE.apply(x, w, targets, tp, real_vocab, seq_parallel)

@@ -1,0 +1,154 @@
+"""Training-step API shared by ``train.py`` and ``bench.py``.
+
+``Trainer(args)`` builds the process grid, the model (``GPT`` / ``GPTStage``
+/ ``GPTChunks``), the schedule, the optimizer and the gradient reducer from a
+``train.py``-style argument namespace, mirroring the reference's
+``train.py:61-110``. One optimisation step is
+
+    zero_grad -> forward/backward (or pipeline train_step) -> DP reduce ->
+    finalize_grads (SP) -> optimizer step
+
+``step_device(idx, tgt)`` runs it on tensors already on the device and returns
+the loss tensor (``None`` off the last stage); ``step(idx, tgt)`` is the end-to-
+end call a user makes: it copies a (pinned) host batch to the device, runs the
+step and reads the loss back to the host.
+"""
+
+from __future__ import annotations
+
+import argparse
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from .models.gpt import GPT, GPTChunks, GPTConfig, GPTStage
+from .optim.precision import MasterWeightOptimizer
+from .parallel import topology
+from .parallel.dp import GradReducer, allreduce_gradients
+from .parallel.pipeline import Pipeline1F1B, PipelineInterleaved
+from .utils.data import SyntheticShard, TokenShard
+
+
+def add_args(p: argparse.ArgumentParser) -> argparse.ArgumentParser:
+    """The reference's ``train.py`` flags (``train.py:29-58``) plus bucket size
+    and checkpointing."""
+    p.add_argument("--tp", type=int, default=1)
+    p.add_argument("--pp", type=int, default=1)
+    p.add_argument("--dp", type=int, default=1)
+    p.add_argument("--chunks", type=int, default=1, help="model chunks per rank (v > 1: interleaved)")
+    p.add_argument("--sp", action="store_true", help="sequence parallelism")
+    p.add_argument("--recompute", action="store_true", help="selective attention recompute")
+    p.add_argument("--bf16", action="store_true", help="bf16 params + fp32 master weights")
+    p.add_argument("--vp", action="store_true", help="vocab-parallel (fused) cross-entropy")
+    p.add_argument("--naive-dp", action="store_true", help="per-parameter blocking all-reduce")
+    p.add_argument("--gpt2", action="store_true", help="GPT-2 124M shape")
+    p.add_argument("--layers", type=int, default=4)
+    p.add_argument("--heads", type=int, default=8)
+    p.add_argument("--embd", type=int, default=128)
+    p.add_argument("--block", type=int, default=64)
+    p.add_argument("--vocab", type=int, default=512)
+    p.add_argument("--data", default="synthetic", help="'synthetic' or a uint16 token file")
+    p.add_argument("--batch", type=int, default=8, help="batch per DP replica")
+    p.add_argument("--micro", type=int, default=1, help="micro batch size (pipeline only)")
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--lr", type=float, default=3e-4)
+    p.add_argument("--seed", type=int, default=1337)
+    p.add_argument("--log-every", type=int, default=1)
+    p.add_argument("--device", default=None, help="cuda|cpu (default: cuda if available)")
+    p.add_argument("--bucket-mb", type=float, default=25.0, help="DP gradient bucket size")
+    p.add_argument("--ckpt-dir", default=None, help="directory for sharded checkpoints")
+    p.add_argument("--ckpt-every", type=int, default=0, help="save every N steps (0: only at the end if --ckpt-dir)")
+    p.add_argument("--resume", action="store_true", help="resume from the latest checkpoint in --ckpt-dir")
+    p.add_argument("--jsonl", default=None, help="append per-step metrics (JSON lines) to this file")
+    return p
+
+
+class Trainer:
+    def __init__(self, args: argparse.Namespace):
+        topology.init_distributed()
+        self.args = args
+        self.tp, self.pp, self.dp = topology.make_topology(args.tp, args.pp, args.dp)
+        self.device = torch.device(args.device) if args.device else topology.default_device()
+        if args.gpt2:
+            args.layers, args.heads, args.embd, args.block, args.vocab = 12, 12, 768, 1024, 50257
+        self.config = GPTConfig(
+            vocab_size=args.vocab,
+            block_size=args.block,
+            n_layer=args.layers,
+            n_head=args.heads,
+            n_embd=args.embd,
+            sequence_parallel=args.sp,
+            recompute_attention=args.recompute,
+            vocab_parallel_loss=args.vp,
+        )
+        cfg = self.config
+        if args.chunks > 1:
+            model = GPTChunks(cfg, self.tp, self.pp, v=args.chunks, seed=args.seed)
+        elif args.pp > 1:
+            model = GPTStage(cfg, self.tp, self.pp, seed=args.seed)
+        else:
+            model = GPT(cfg, self.tp, seed=args.seed)
+        model = model.to(self.device)
+        if args.bf16:
+            model = model.to(torch.bfloat16)
+        self.model = model
+        if args.chunks > 1:
+            self.pipe = PipelineInterleaved(model, self.pp, micro_batch_size=args.micro, seq_len=cfg.block_size)
+        elif args.pp > 1:
+            self.pipe = Pipeline1F1B(model, self.pp, micro_batch_size=args.micro, seq_len=cfg.block_size)
+        else:
+            self.pipe = None
+        if args.bf16:
+            self.opt = MasterWeightOptimizer(model.parameters(), lr=args.lr)
+        else:
+            self.opt = torch.optim.Adam(model.parameters(), lr=args.lr)
+        self.reducer = None
+        if self.dp.enabled and not args.naive_dp:
+            self.reducer = GradReducer(
+                model, self.dp, bucket_bytes=int(args.bucket_mb * 1024 * 1024), overlap=self.pipe is None
+            )
+        if args.data == "synthetic":
+            self.shard = SyntheticShard(cfg.vocab_size, cfg.block_size, args.batch, seed=args.seed, dp=self.dp)
+        else:
+            self.shard = TokenShard(args.data, cfg.block_size, args.batch, seed=args.seed, dp=self.dp)
+        self.tokens_per_step = args.batch * cfg.block_size * args.dp
+        self.is_logger = self.pp.is_last and self.tp.rank == 0 and self.dp.rank == 0
+        self.step_index = 0
+
+    @property
+    def n_params(self) -> int:
+        return sum(p.numel() for p in self.model.parameters())
+
+    def step_device(self, idx: torch.Tensor, tgt: torch.Tensor) -> Optional[torch.Tensor]:
+        self.opt.zero_grad(set_to_none=True)
+        if self.pipe is not None:
+            loss = self.pipe.train_step(idx, tgt)
+            if self.reducer is not None:
+                self.reducer.reduce()
+        else:
+            _, loss = self.model(idx, tgt)
+            loss.backward()
+        if self.reducer is not None:
+            self.reducer.finish()
+        elif self.dp.enabled:
+            allreduce_gradients(self.model, self.dp)
+        self.model.finalize_grads()
+        self.opt.step()
+        self.step_index += 1
+        return loss
+
+    def step(self, idx: torch.Tensor, tgt: torch.Tensor) -> Optional[float]:
+        """End-to-end step from host tensors; returns the local loss (host
+        float) on the last pipeline stage, None elsewhere."""
+        idx = idx.to(self.device, non_blocking=True)
+        tgt = tgt.to(self.device, non_blocking=True)
+        loss = self.step_device(idx, tgt)
+        return None if loss is None else float(loss.detach().float().item())
+
+    def dp_mean_loss(self, loss: torch.Tensor) -> torch.Tensor:
+        avg = loss.detach().float().clone()
+        if self.dp.enabled:
+            dist.all_reduce(avg, group=self.dp.group)
+            avg /= self.dp.world
+        return avg
