@@ -1,6 +1,6 @@
 // Host side of the tcgen05 GEMM: TMA descriptor encoding, tile-shape and
 // split-K selection, launch; plus the deterministic split-K reduction and
-// the column-sum (bias gradient) kernels.
+// the column-sum (bias gradient) entry.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
@@ -9,6 +9,7 @@
 
 #include "common.h"
 #include "gemm.cuh"
+#include "reduce.cuh"
 
 namespace dst {
 
@@ -182,32 +183,6 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, s
   }
 }
 
-// Column sums of a bf16 [M, N] matrix: stage 1 writes per-row-block fp32
-// partials [R, N]; stage 2 sums them in row-block order.
-__global__ void colsum_stage1(const __nv_bfloat16* __restrict__ x, int M, int N, int rows_per_block,
-                              float* __restrict__ partial) {
-  const int col2 = blockIdx.x * blockDim.x + threadIdx.x;  // column pair index
-  if (col2 * 2 >= N) return;
-  const int r0 = blockIdx.y * rows_per_block;
-  const int r1 = min(M, r0 + rows_per_block);
-  float a = 0.f, b = 0.f;
-  for (int r = r0; r < r1; ++r) {
-    float2 f = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(x + static_cast<size_t>(r) * N)[col2]);
-    a += f.x;
-    b += f.y;
-  }
-  partial[static_cast<size_t>(blockIdx.y) * N + col2 * 2] = a;
-  partial[static_cast<size_t>(blockIdx.y) * N + col2 * 2 + 1] = b;
-}
-
-__global__ void colsum_stage2(const float* __restrict__ partial, int R, int N, __nv_bfloat16* __restrict__ out) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= N) return;
-  float s = 0.f;
-  for (int r = 0; r < R; ++r) s += partial[static_cast<size_t>(r) * N + c];
-  out[c] = __float2bfloat16_rn(s);
-}
-
 }  // namespace dst
 
 // ---------------------------------------------------------------- bindings
@@ -301,22 +276,22 @@ at::Tensor gemm_splitk(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool
   return out;
 }
 
+// Column sums (bias gradient) via the deterministic two-pass reduction.
 at::Tensor colsum_bf16(const at::Tensor& x) {
   check_bf16_2d(x, "x");
   TORCH_CHECK(x.is_contiguous(), "colsum: contiguous input required");
   c10::cuda::CUDAGuard g(x.device());
   const int M = x.size(0), N = x.size(1);
-  TORCH_CHECK(N % 2 == 0, "colsum: N must be even");
-  const int rows_per_block = 64;
-  const int R = (M + rows_per_block - 1) / rows_per_block;
+  TORCH_CHECK(N % 8 == 0, "colsum: N must be a multiple of 8");
+  const int R = (M + kColredRows - 1) / kColredRows;
   at::Tensor partial = at::empty({R, N}, x.options().dtype(at::kFloat));
   at::Tensor out = at::empty({N}, x.options());
   auto st = at::cuda::getCurrentCUDAStream();
-  dim3 g1((N / 2 + 127) / 128, R);
-  colsum_stage1<<<g1, 128, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), M, N, rows_per_block,
-                                    partial.data_ptr<float>());
-  colsum_stage2<<<(N + 255) / 256, 256, 0, st>>>(partial.data_ptr<float>(), R, N,
-                                                 reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
+  dim3 g1((N + 255) / 256, R);
+  colred_stage1<false><<<g1, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), nullptr, nullptr,
+                                           nullptr, M, N, partial.data_ptr<float>(), nullptr);
+  dim3 g2((N + 31) / 32, 1);
+  colred_stage2<<<g2, 256, 0, st>>>(partial.data_ptr<float>(), R, N, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return out;
 }

@@ -5,17 +5,16 @@
 // deviations) and the fp32 mean / rstd are saved for backward.
 //
 // Backward: one warp per row computes
-//   dx = rstd * (g - mean(g) - xhat * mean(g * xhat)),  g = w * dy
-// and accumulates dγ = Σ dy·xhat, dβ = Σ dy for its columns in registers
-// across the rows its CTA owns; the CTA's warps are combined in shared memory
-// in warp order and written as one fp32 partial row per CTA, which a second
-// kernel sums in CTA order. Deterministic: no atomics anywhere.
+//   dx = rstd * (g - mean(g) - xhat * mean(g * xhat)),  g = w * dy;
+// dγ = Σ dy·xhat and dβ = Σ dy are deterministic two-pass column reductions
+// (reduce.cuh). No atomics anywhere.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
 #include "common.h"
 #include "ptx.cuh"
+#include "reduce.cuh"
 
 namespace dst {
 
@@ -99,105 +98,67 @@ __global__ void ln_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bf
   }
 }
 
+// dx only: one warp per row, x and dy kept packed (bf16) in registers, the
+// weight re-read through L1. dγ/dβ come from the column reduction in
+// reduce.cuh, which re-reads x and dy; splitting the two keeps this kernel's
+// register footprint small enough for full occupancy.
 template <int MAXV>
-__global__ void ln_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
-                              const __nv_bfloat16* __restrict__ w, const float* __restrict__ mean,
-                              const float* __restrict__ rstd, __nv_bfloat16* __restrict__ dx,
-                              float* __restrict__ part_dw, float* __restrict__ part_db, int rows, int C,
-                              int rows_per_block) {
-  extern __shared__ float red[];  // [2][C]
+__global__ void __launch_bounds__(256) ln_bwd_dx_kernel(const __nv_bfloat16* __restrict__ dy,
+                                                        const __nv_bfloat16* __restrict__ x,
+                                                        const __nv_bfloat16* __restrict__ w,
+                                                        const float* __restrict__ mean, const float* __restrict__ rstd,
+                                                        __nv_bfloat16* __restrict__ dx, int rows, int C) {
   const int warps = blockDim.x >> 5;
-  const int warp = threadIdx.x >> 5;
+  const int row = blockIdx.x * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
   const int nvec = C >> 3;
-  float adw[MAXV][8], adb[MAXV][8];
-  float wf[MAXV][8];
+  const uint4* xr = reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * C);
+  const uint4* gr = reinterpret_cast<const uint4*>(dy + static_cast<size_t>(row) * C);
   const uint4* wv = reinterpret_cast<const uint4*>(w);
+  uint4 xp[MAXV], gp[MAXV];
 #pragma unroll
   for (int i = 0; i < MAXV; ++i) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) adw[i][j] = adb[i][j] = 0.f;
-    if (lane + 32 * i < nvec) unpack8(wv[lane + 32 * i], wf[i]);
-  }
-  const int r0 = blockIdx.x * rows_per_block;
-  const int r1 = min(rows, r0 + rows_per_block);
-  for (int row = r0 + warp; row < r1; row += warps) {
-    const uint4* xr = reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * C);
-    const uint4* gr = reinterpret_cast<const uint4*>(dy + static_cast<size_t>(row) * C);
-    const float mu = mean[row], rs = rstd[row];
-    float xh[MAXV][8], g[MAXV][8];
-    float s1 = 0.f, s2 = 0.f;
-#pragma unroll
-    for (int i = 0; i < MAXV; ++i) {
-      const int vi = lane + 32 * i;
-      if (vi < nvec) {
-        float xf[8], df[8];
-        unpack8(xr[vi], xf);
-        unpack8(gr[vi], df);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          xh[i][j] = (xf[j] - mu) * rs;
-          g[i][j] = df[j] * wf[i][j];
-          s1 += g[i][j];
-          s2 += g[i][j] * xh[i][j];
-          adw[i][j] += df[j] * xh[i][j];
-          adb[i][j] += df[j];
-        }
-      }
+    const int vi = lane + 32 * i;
+    if (vi < nvec) {
+      xp[i] = xr[vi];
+      gp[i] = gr[vi];
     }
-    s1 = warp_sum(s1) / C;
-    s2 = warp_sum(s2) / C;
-    uint4* dxr = reinterpret_cast<uint4*>(dx + static_cast<size_t>(row) * C);
+  }
+  const float mu = mean[row], rs = rstd[row];
+  float s1 = 0.f, s2 = 0.f;
 #pragma unroll
-    for (int i = 0; i < MAXV; ++i) {
-      const int vi = lane + 32 * i;
-      if (vi < nvec) {
-        float o[8];
+  for (int i = 0; i < MAXV; ++i) {
+    const int vi = lane + 32 * i;
+    if (vi < nvec) {
+      float xf[8], df[8], wf[8];
+      unpack8(xp[i], xf);
+      unpack8(gp[i], df);
+      unpack8(__ldg(wv + vi), wf);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] = rs * (g[i][j] - s1 - xh[i][j] * s2);
-        dxr[vi] = pack8(o);
+      for (int j = 0; j < 8; ++j) {
+        const float g = df[j] * wf[j];
+        s1 += g;
+        s2 += g * (xf[j] - mu) * rs;
       }
     }
   }
-  // Combine the warps of this CTA in warp order (sequential adds into one
-  // shared row pair keep the order fixed without per-warp copies).
-  float* acc_w = red;
-  float* acc_b = red + C;
-  for (int c = threadIdx.x; c < 2 * C; c += blockDim.x) red[c] = 0.f;
-  __syncthreads();
-  for (int k = 0; k < warps; ++k) {
-    if (warp == k) {
+  s1 = warp_sum(s1) / C;
+  s2 = warp_sum(s2) / C;
+  uint4* dxr = reinterpret_cast<uint4*>(dx + static_cast<size_t>(row) * C);
 #pragma unroll
-      for (int i = 0; i < MAXV; ++i) {
-        const int vi = lane + 32 * i;
-        if (vi < nvec) {
+  for (int i = 0; i < MAXV; ++i) {
+    const int vi = lane + 32 * i;
+    if (vi < nvec) {
+      float xf[8], df[8], wf[8], o[8];
+      unpack8(xp[i], xf);
+      unpack8(gp[i], df);
+      unpack8(__ldg(wv + vi), wf);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            acc_w[vi * 8 + j] += adw[i][j];
-            acc_b[vi * 8 + j] += adb[i][j];
-          }
-        }
-      }
+      for (int j = 0; j < 8; ++j) o[j] = rs * (df[j] * wf[j] - s1 - (xf[j] - mu) * rs * s2);
+      dxr[vi] = pack8(o);
     }
-    __syncthreads();
   }
-  for (int c = threadIdx.x; c < C; c += blockDim.x) {
-    part_dw[static_cast<size_t>(blockIdx.x) * C + c] = acc_w[c];
-    part_db[static_cast<size_t>(blockIdx.x) * C + c] = acc_b[c];
-  }
-}
-
-__global__ void sum_partials_kernel(const float* __restrict__ pw, const float* __restrict__ pb, int R, int C,
-                                    __nv_bfloat16* __restrict__ dw, __nv_bfloat16* __restrict__ db) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= C) return;
-  float a = 0.f, b = 0.f;
-  for (int r = 0; r < R; ++r) {
-    a += pw[static_cast<size_t>(r) * C + c];
-    b += pb[static_cast<size_t>(r) * C + c];
-  }
-  dw[c] = __float2bfloat16_rn(a);
-  db[c] = __float2bfloat16_rn(b);
 }
 
 }  // namespace dst
@@ -243,25 +204,22 @@ std::vector<at::Tensor> layernorm_bwd(const at::Tensor& dy, const at::Tensor& x,
   c10::cuda::CUDAGuard g(x.device());
   const int rows = x.size(0), C = x.size(1);
   at::Tensor dx = at::empty_like(x);
-  const int threads = 256, warps = threads / 32;
-  const int sms = num_sms();
-  // Enough CTAs to fill the GPU a few times over, each owning a row range.
-  int rows_per_block = std::max(warps, (rows + 4 * sms - 1) / (4 * sms));
-  const int R = (rows + rows_per_block - 1) / rows_per_block;
-  at::Tensor pw = at::empty({R, C}, x.options().dtype(at::kFloat));
-  at::Tensor pb = at::empty({R, C}, x.options().dtype(at::kFloat));
-  at::Tensor dw = at::empty({C}, x.options());
-  at::Tensor db = at::empty({C}, x.options());
-  const size_t smem = 2 * static_cast<size_t>(C) * sizeof(float);
-  TORCH_CHECK(smem <= 48 * 1024, "layernorm_bwd: hidden size too large");
   auto st = at::cuda::getCurrentCUDAStream();
-  LN_DISPATCH(C, ln_bwd_kernel, <<<R, threads, smem, st>>>(cbf(dy), cbf(x), cbf(w), mean.data_ptr<float>(),
-                                                           rstd.data_ptr<float>(), bf(dx), pw.data_ptr<float>(),
-                                                           pb.data_ptr<float>(), rows, C, rows_per_block));
+  const int threads = 256, per = threads / 32;
+  LN_DISPATCH(C, ln_bwd_dx_kernel, <<<(rows + per - 1) / per, threads, 0, st>>>(
+                                       cbf(dy), cbf(x), cbf(w), mean.data_ptr<float>(), rstd.data_ptr<float>(), bf(dx),
+                                       rows, C));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  sum_partials_kernel<<<(C + 255) / 256, 256, 0, st>>>(pw.data_ptr<float>(), pb.data_ptr<float>(), R, C, bf(dw), bf(db));
+  const int R = (rows + kColredRows - 1) / kColredRows;
+  at::Tensor part = at::empty({2, R, C}, x.options().dtype(at::kFloat));
+  at::Tensor dwb = at::empty({2, C}, x.options());
+  dim3 g1((C + 255) / 256, R);
+  colred_stage1<true><<<g1, 256, 0, st>>>(cbf(dy), cbf(x), mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, C,
+                                          part.data_ptr<float>(), part.data_ptr<float>() + static_cast<size_t>(R) * C);
+  dim3 g2((C + 31) / 32, 2);
+  colred_stage2<<<g2, 256, 0, st>>>(part.data_ptr<float>(), R, C, bf(dwb));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  return {dx, dw, db};
+  return {dx, dwb[0], dwb[1]};
 }
 
 void register_norm(pybind11::module& m) {

@@ -1,0 +1,222 @@
+"""Sharded, reshardable checkpoints.
+
+Layout of one checkpoint (a directory per step)::
+
+    <root>/step_00000100/
+        manifest.json              config, topology, step, seed, tensor index
+        shard_tp{t}_pp{p}.pt       {global name: local tensor} for one (tp, pp) cell,
+                                   model weights plus optimizer state
+        COMPLETE                   written last by rank 0: the checkpoint is whole
+
+Each (tp, pp) cell is written by its data-parallel rank 0 (DP replicas hold
+identical weights and optimizer state). Tensors are keyed by their GLOBAL
+name - the parameter name in the full single-process model (via
+``ref_param_name``) prefixed with ``model/``, ``master/``, ``exp_avg/`` or
+``exp_avg_sq/`` - and the manifest records, per global name, the full shape
+and how it is split across TP ranks (dimension, or ``null`` when
+replicated) and which pipeline stage holds it. Because initialisation and
+naming are decomposition-invariant, loading into a different TP/PP layout is
+a concatenate-then-slice: a checkpoint written at tp=2 x pp=2 loads at tp=1 or
+tp=4 unchanged. Data needs no state: batches are a pure function of (seed,
+step, dp rank).
+
+The reference has no checkpointing; this format is new.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+from typing import Dict, Optional
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+
+from ..models.layers import ColumnParallelLinear, RowParallelLinear
+
+STATE_KINDS = ("master", "exp_avg", "exp_avg_sq")
+
+
+def split_dim(model: nn.Module, local_name: str) -> Optional[int]:
+    """TP split dimension of a parameter (None when replicated)."""
+    owner = model.get_submodule(local_name.rsplit(".", 1)[0]) if "." in local_name else model
+    leaf = local_name.rsplit(".", 1)[-1]
+    if isinstance(owner, ColumnParallelLinear):
+        return 0
+    if isinstance(owner, RowParallelLinear) and leaf == "weight":
+        return 1
+    return None
+
+
+def _global_name(model: nn.Module, name: str) -> str:
+    fn = getattr(model, "ref_param_name", None)
+    return fn(name) if fn else name
+
+
+def _optimizer_state(opt, params):
+    """Per-parameter fp32 state tensors: master weights and Adam moments when
+    the optimizer keeps them; ``step`` as a float."""
+    from ..optim.precision import MasterWeightOptimizer
+
+    out = {}
+    step = 0.0
+    if isinstance(opt, MasterWeightOptimizer):
+        by_param = dict(zip([id(p) for p in opt.model_params], opt.master_params))
+        for name, p in params:
+            m = by_param.get(id(p))
+            if m is None:
+                continue
+            st = opt.inner.state.get(m, {})
+            out[name] = {"master": m}
+            if st:
+                out[name]["exp_avg"] = st["exp_avg"]
+                out[name]["exp_avg_sq"] = st["exp_avg_sq"]
+                step = float(st["step"])
+    elif isinstance(opt, torch.optim.Optimizer):
+        for name, p in params:
+            st = opt.state.get(p, {})
+            if st:
+                out[name] = {"exp_avg": st["exp_avg"], "exp_avg_sq": st["exp_avg_sq"]}
+                step = float(st["step"])
+    return out, step
+
+
+def save(root: str, step: int, model: nn.Module, opt, tp, pp, dp, config, seed: int, extra: Optional[dict] = None) -> str:
+    path = os.path.join(root, f"step_{step:08d}")
+    rank = dist.get_rank() if dist.is_initialized() else 0
+    if rank == 0:
+        os.makedirs(path, exist_ok=True)
+    if dist.is_initialized():
+        dist.barrier()
+    params = list(model.named_parameters())
+    state, opt_step = _optimizer_state(opt, params)
+    index: Dict[str, dict] = {}
+    tensors: Dict[str, torch.Tensor] = {}
+    for name, p in params:
+        g = _global_name(model, name)
+        d = split_dim(model, name)
+        full = list(p.shape)
+        if d is not None:
+            full[d] *= tp.world
+        index[f"model/{g}"] = {"shape": full, "split_dim": d, "pp": pp.rank, "dtype": str(p.dtype)}
+        tensors[f"model/{g}"] = p.detach().cpu()
+        for kind, t in state.get(name, {}).items():
+            index[f"{kind}/{g}"] = {"shape": full, "split_dim": d, "pp": pp.rank, "dtype": str(t.dtype)}
+            tensors[f"{kind}/{g}"] = t.detach().cpu()
+    if dp.rank == 0:
+        torch.save(tensors, os.path.join(path, f"shard_tp{tp.rank}_pp{pp.rank}.pt"))
+    # Gather every cell's index on rank 0 for the manifest.
+    gathered = [None] * (dist.get_world_size() if dist.is_initialized() else 1)
+    if dist.is_initialized():
+        dist.all_gather_object(gathered, index if dp.rank == 0 and tp.rank == 0 else None)
+    else:
+        gathered = [index]
+    if rank == 0:
+        merged = {}
+        for part in gathered:
+            if part:
+                merged.update(part)
+        manifest = {
+            "format": "dstraining_b200/sharded-v1",
+            "step": step,
+            "seed": seed,
+            "optimizer_step": opt_step,
+            "config": dict(vars(config)),
+            "topology": {"tp": tp.world, "pp": pp.world, "dp": dp.world},
+            "tensors": merged,
+            "extra": extra or {},
+        }
+        with open(os.path.join(path, "manifest.json"), "w") as f:
+            json.dump(manifest, f, indent=1, sort_keys=True)
+    if dist.is_initialized():
+        dist.barrier()
+    if rank == 0:
+        with open(os.path.join(path, "COMPLETE"), "w") as f:
+            f.write("ok\n")
+    if dist.is_initialized():
+        dist.barrier()
+    return path
+
+
+def latest(root: str) -> Optional[str]:
+    if not os.path.isdir(root):
+        return None
+    steps = sorted(d for d in os.listdir(root) if d.startswith("step_") and os.path.exists(os.path.join(root, d, "COMPLETE")))
+    return os.path.join(root, steps[-1]) if steps else None
+
+
+class _Reader:
+    """Loads global tensors from a checkpoint written at any topology."""
+
+    def __init__(self, path: str):
+        self.path = path
+        with open(os.path.join(path, "manifest.json")) as f:
+            self.manifest = json.load(f)
+        self.topo = self.manifest["topology"]
+        self._cache: Dict[str, dict] = {}
+
+    def _file(self, t: int, p: int) -> dict:
+        key = f"shard_tp{t}_pp{p}.pt"
+        if key not in self._cache:
+            self._cache[key] = torch.load(os.path.join(self.path, key), map_location="cpu", weights_only=True)
+        return self._cache[key]
+
+    def full(self, key: str) -> Optional[torch.Tensor]:
+        meta = self.manifest["tensors"].get(key)
+        if meta is None:
+            return None
+        if meta["split_dim"] is None:
+            return self._file(0, meta["pp"])[key]
+        parts = [self._file(t, meta["pp"])[key] for t in range(self.topo["tp"])]
+        return torch.cat(parts, dim=meta["split_dim"])
+
+
+def load(path: str, model: nn.Module, opt, tp) -> dict:
+    """Load weights (and optimizer state when present) into this rank's
+    model/optimizer, resharding as needed. Returns the manifest."""
+    from ..optim.precision import MasterWeightOptimizer
+
+    rd = _Reader(path)
+    params = list(model.named_parameters())
+    masters = {}
+    if isinstance(opt, MasterWeightOptimizer):
+        masters = dict(zip([id(p) for p in opt.model_params], opt.master_params))
+
+    def local(key, name, like):
+        full = rd.full(key)
+        if full is None:
+            return None
+        d = split_dim(model, name)
+        if d is not None:
+            n = like.shape[d]
+            full = full.narrow(d, tp.rank * n, n)
+        return full
+
+    opt_step = float(rd.manifest.get("optimizer_step", 0.0))
+    with torch.no_grad():
+        for name, p in params:
+            g = _global_name(model, name)
+            w = local(f"model/{g}", name, p)
+            if w is None:
+                raise KeyError(f"checkpoint {path} has no tensor for {g}")
+            p.copy_(w.to(p.dtype))
+            if isinstance(opt, MasterWeightOptimizer) and id(p) in masters:
+                m = masters[id(p)]
+                src = local(f"master/{g}", name, p)
+                m.copy_(src if src is not None else w.float())
+                ea, eas = local(f"exp_avg/{g}", name, p), local(f"exp_avg_sq/{g}", name, p)
+                if ea is not None and eas is not None:
+                    st = opt._state(m)
+                    st["exp_avg"].copy_(ea)
+                    st["exp_avg_sq"].copy_(eas)
+                    st["step"] = torch.tensor(opt_step)
+            elif isinstance(opt, torch.optim.Optimizer):
+                ea, eas = local(f"exp_avg/{g}", name, p), local(f"exp_avg_sq/{g}", name, p)
+                if ea is not None and eas is not None:
+                    opt.state[p] = {
+                        "step": torch.tensor(opt_step),
+                        "exp_avg": ea.to(p.device, p.dtype).clone(),
+                        "exp_avg_sq": eas.to(p.device, p.dtype).clone(),
+                    }
+    return rd.manifest

@@ -66,3 +66,23 @@ def test_recompute_suite():
     env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
     r = subprocess.run([sys.executable, os.path.join(SUITES, "recompute_suite.py")], env=env, timeout=300)
     assert r.returncode == 0
+
+
+@pytest.mark.parametrize("n,args", [(2, ("--tp", "2")), (4, ("--tp", "2", "--pp", "2"))])
+def test_checkpoint_suite(n, args, tmp_path):
+    run(n, "ckpt_suite.py", *args, "--dir", str(tmp_path / "ckpt"))
+
+
+def test_train_cli_all_axes_and_resume(tmp_path):
+    """train.py with dp x pp x tp x interleaving x SP on 8 gloo ranks, then a
+    resume from its checkpoint."""
+    root = os.path.dirname(SUITES)
+    train = os.path.join(os.path.dirname(root), "train.py")
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="1")
+    ck = str(tmp_path / "ck")
+    common = ["--dp", "2", "--pp", "2", "--tp", "2", "--chunks", "2", "--sp", "--recompute", "--vp",
+              "--micro", "1", "--batch", "4", "--device", "cpu", "--ckpt-dir", ck, "--jsonl", str(tmp_path / "m.jsonl")]
+    assert launch(8, [train, "--steps", "4", *common], timeout=540, env=env) == 0
+    assert launch(8, [train, "--steps", "6", "--resume", *common], timeout=540, env=env) == 0
+    lines = open(tmp_path / "m.jsonl").read().splitlines()
+    assert len(lines) == 6  # steps 0-3, then 4-5 after the resume

@@ -1,0 +1,78 @@
+"""Train a GPT with any composition of tp x pp x dp, interleaving, sequence
+parallelism, selective recompute and bf16 + fp32 master weights.
+
+    # CPU smoke test, all axes at once (8 gloo ranks):
+    python -m dstraining_b200.utils.launch 8 train.py --dp 2 --pp 2 --tp 2 --chunks 2 \
+        --sp --recompute --steps 20 --data synthetic
+    # 8 B200s, GPT-2 124M data parallel, bf16 + fp32 masters:
+    torchrun --nproc_per_node 8 train.py --dp 8 --bf16 --vp --gpt2 --batch 16 --vocab 50304
+
+Same flags as the reference's ``train.py:29-58`` (plus ``--bucket-mb``,
+checkpointing and ``--jsonl``). Logs ``step N  loss X  T tok/s`` from the
+last pipeline stage's tp0/dp0 rank; the loss is averaged over DP and the
+throughput is over the steps since the previous log line, measured with the
+device synchronised.
+"""
+
+import argparse
+import json
+import sys
+import time
+
+import torch
+import torch.distributed as dist
+
+from dstraining_b200.trainer import Trainer, add_args
+from dstraining_b200.utils import checkpoint
+
+
+def main():
+    args = add_args(argparse.ArgumentParser()).parse_args()
+    tr = Trainer(args)
+    start_step = 0
+    if args.resume and args.ckpt_dir:
+        path = checkpoint.latest(args.ckpt_dir)
+        if path:
+            manifest = checkpoint.load(path, tr.model, tr.opt, tr.tp)
+            start_step = int(manifest["step"])
+            if tr.is_logger:
+                print(f"resumed from {path} at step {start_step}", flush=True)
+    if tr.is_logger:
+        print(
+            f"tp={args.tp} pp={args.pp} dp={args.dp} chunks={args.chunks} sp={args.sp} "
+            f"recompute={args.recompute} bf16={args.bf16} vp={args.vp} device={tr.device.type} | "
+            f"{tr.n_params:,} params this rank | batch {args.batch}/replica",
+            flush=True,
+        )
+    sink = open(args.jsonl, "a") if (args.jsonl and tr.is_logger) else None
+    cuda = tr.device.type == "cuda"
+    t_last, s_last = time.time(), start_step
+    for step in range(start_step, args.steps):
+        idx, tgt = tr.shard.get_batch(step, pin=cuda)
+        loss = tr.step_device(idx.to(tr.device, non_blocking=True), tgt.to(tr.device, non_blocking=True))
+        last = step == args.steps - 1
+        if tr.pp.is_last and (step % args.log_every == 0 or last):
+            avg = tr.dp_mean_loss(loss)
+            if tr.is_logger:
+                value = avg.item()  # synchronises the device
+                now = time.time()
+                tps = tr.tokens_per_step * (step + 1 - s_last) / max(now - t_last, 1e-9)
+                print(f"step {step:5d}  loss {value:.4f}  {tps:,.0f} tok/s", flush=True)
+                if sink:
+                    sink.write(json.dumps({"step": step, "loss": value, "tok_s": tps}) + "\n")
+                    sink.flush()
+                t_last, s_last = now, step + 1
+        if args.ckpt_dir and args.ckpt_every and (step + 1) % args.ckpt_every == 0 and not last:
+            checkpoint.save(args.ckpt_dir, step + 1, tr.model, tr.opt, tr.tp, tr.pp, tr.dp, tr.config, args.seed)
+    if args.ckpt_dir:
+        checkpoint.save(args.ckpt_dir, args.steps, tr.model, tr.opt, tr.tp, tr.pp, tr.dp, tr.config, args.seed)
+    if sink:
+        sink.close()
+    if dist.is_initialized():
+        dist.barrier()
+        dist.destroy_process_group()
+    sys.exit(0)
+
+
+if __name__ == "__main__":
+    main()
