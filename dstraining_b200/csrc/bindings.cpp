@@ -43,4 +43,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_adam(m);
   register_ce(m);
   register_attn(m);
+  register_attn_tc(m);
 }

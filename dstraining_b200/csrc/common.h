@@ -26,3 +26,4 @@ void register_embed(pybind11::module& m);
 void register_adam(pybind11::module& m);
 void register_ce(pybind11::module& m);
 void register_attn(pybind11::module& m);
+void register_attn_tc(pybind11::module& m);

@@ -59,7 +59,8 @@ int num_sms() {
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
-static void launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid, cudaStream_t st) {
+static void launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const CUtensorMap& tx,
+                       const GemmParams& p, int grid, cudaStream_t st) {
   auto kern = gemm_bf16_kernel<BN, A_MN, B_MN, EPI>;
   constexpr int smem = GemmCfg<BN>::kSmemBytes;
   static bool configured[64] = {false};
@@ -69,33 +70,34 @@ static void launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmP
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     configured[dev] = true;
   }
-  kern<<<grid, kGemmThreads, smem, st>>>(ta, tb, p);
+  kern<<<grid, kGemmThreads, smem, st>>>(ta, tb, to, tx, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 template <int BN, bool A_MN, bool B_MN>
-static void dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid,
-                         cudaStream_t st) {
+static void dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+                         const CUtensorMap& tx, const GemmParams& p, int grid, cudaStream_t st) {
   switch (epi) {
-    case kEpiStore: return launch_one<BN, A_MN, B_MN, kEpiStore>(ta, tb, p, grid, st);
-    case kEpiBias: return launch_one<BN, A_MN, B_MN, kEpiBias>(ta, tb, p, grid, st);
-    case kEpiBiasGelu: return launch_one<BN, A_MN, B_MN, kEpiBiasGelu>(ta, tb, p, grid, st);
-    case kEpiBiasResid: return launch_one<BN, A_MN, B_MN, kEpiBiasResid>(ta, tb, p, grid, st);
-    case kEpiDGelu: return launch_one<BN, A_MN, B_MN, kEpiDGelu>(ta, tb, p, grid, st);
-    case kEpiPartialF32: return launch_one<BN, A_MN, B_MN, kEpiPartialF32>(ta, tb, p, grid, st);
-    case kEpiCEStats: return launch_one<BN, A_MN, B_MN, kEpiCEStats>(ta, tb, p, grid, st);
-    case kEpiAccumF32: return launch_one<BN, A_MN, B_MN, kEpiAccumF32>(ta, tb, p, grid, st);
+    case kEpiStore: return launch_one<BN, A_MN, B_MN, kEpiStore>(ta, tb, to, tx, p, grid, st);
+    case kEpiBias: return launch_one<BN, A_MN, B_MN, kEpiBias>(ta, tb, to, tx, p, grid, st);
+    case kEpiBiasGelu: return launch_one<BN, A_MN, B_MN, kEpiBiasGelu>(ta, tb, to, tx, p, grid, st);
+    case kEpiBiasResid: return launch_one<BN, A_MN, B_MN, kEpiBiasResid>(ta, tb, to, tx, p, grid, st);
+    case kEpiDGelu: return launch_one<BN, A_MN, B_MN, kEpiDGelu>(ta, tb, to, tx, p, grid, st);
+    case kEpiPartialF32: return launch_one<BN, A_MN, B_MN, kEpiPartialF32>(ta, tb, to, tx, p, grid, st);
+    case kEpiCEStats: return launch_one<BN, A_MN, B_MN, kEpiCEStats>(ta, tb, to, tx, p, grid, st);
+    case kEpiAccumF32: return launch_one<BN, A_MN, B_MN, kEpiAccumF32>(ta, tb, to, tx, p, grid, st);
     default: TORCH_CHECK(false, "unknown epilogue ", epi);
   }
 }
 
 template <int BN>
 static void dispatch_layout(bool a_mn, bool b_mn, int epi, const CUtensorMap& ta, const CUtensorMap& tb,
-                            const GemmParams& p, int grid, cudaStream_t st) {
-  if (!a_mn && !b_mn) return dispatch_epi<BN, false, false>(epi, ta, tb, p, grid, st);
-  if (!a_mn && b_mn) return dispatch_epi<BN, false, true>(epi, ta, tb, p, grid, st);
-  if (a_mn && b_mn) return dispatch_epi<BN, true, true>(epi, ta, tb, p, grid, st);
-  return dispatch_epi<BN, true, false>(epi, ta, tb, p, grid, st);
+                            const CUtensorMap& to, const CUtensorMap& tx, const GemmParams& p, int grid,
+                            cudaStream_t st) {
+  if (!a_mn && !b_mn) return dispatch_epi<BN, false, false>(epi, ta, tb, to, tx, p, grid, st);
+  if (!a_mn && b_mn) return dispatch_epi<BN, false, true>(epi, ta, tb, to, tx, p, grid, st);
+  if (a_mn && b_mn) return dispatch_epi<BN, true, true>(epi, ta, tb, to, tx, p, grid, st);
+  return dispatch_epi<BN, true, false>(epi, ta, tb, to, tx, p, grid, st);
 }
 
 // Pick the number of K splits: minimise waves / splits (time per unit of K)
@@ -141,10 +143,17 @@ void gemm_run(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, in
   const int units = tiles * splits;
   const int grid = std::min(units, sms);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  // bf16 outputs are written by TMA stores of 32x64 boxes.
+  CUtensorMap to = ta, tx = ta;
+  if (epi != kEpiPartialF32 && epi != kEpiAccumF32) {
+    TORCH_CHECK(p.out != nullptr, "gemm: missing output");
+    to = make_tmap_bf16(p.out, N, M, p.ldo, kEpiChunk, 32);
+    if (epi == kEpiBiasGelu) tx = make_tmap_bf16(p.aux_out, N, M, p.ldo, kEpiChunk, 32);
+  }
   if (BN == 256)
-    dispatch_layout<256>(a_mn, b_mn, epi, ta, tb, p, grid, st);
+    dispatch_layout<256>(a_mn, b_mn, epi, ta, tb, to, tx, p, grid, st);
   else
-    dispatch_layout<128>(a_mn, b_mn, epi, ta, tb, p, grid, st);
+    dispatch_layout<128>(a_mn, b_mn, epi, ta, tb, to, tx, p, grid, st);
 }
 
 int gemm_splits_for(int M, int N, int K) {

@@ -15,8 +15,14 @@
 //               tcgen05.mma (M=128, N=BN, K=16) x 4 per 64-wide K stage and
 //               tcgen05.commit's the stage back to the producer; after a
 //               tile's last stage it commits the accumulator to the epilogue.
-//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time (one TMEM lane =
-//               one output row per thread), apply the fused epilogue, store.
+//   warps 2..5  epilogue: each warp owns 32 TMEM lanes (= 32 output rows).
+//               Per 64-column chunk it reads the accumulator with
+//               tcgen05.ld, applies the fused epilogue, writes the bf16
+//               chunk into a 128B-swizzled 32x64 staging tile in shared
+//               memory and one lane issues a TMA bulk-tensor store (two
+//               staging tiles per warp, so a store drains while the next
+//               chunk is computed). fp32 epilogues (split-K partials,
+//               accumulation) store straight from registers.
 // The accumulator is double-buffered in TMEM (2 x BN fp32 columns), so the
 // epilogue of tile i overlaps the MMAs of tile i+1.
 //
@@ -64,6 +70,8 @@ struct GemmParams {
 constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kGemmThreads = 192;
+constexpr int kEpiChunk = 64;                        // columns per epilogue chunk
+constexpr int kStageTileBytes = 32 * kEpiChunk * 2;  // one 32x64 bf16 staging tile
 
 template <int BN>
 struct GemmCfg {
@@ -72,25 +80,11 @@ struct GemmCfg {
   static constexpr int kStageBytes = kStageA + kStageB;
   static constexpr int kStages = (BN == 256) ? 4 : 6;
   static constexpr int kTmemCols = 2 * BN;  // power of two: 256 or 512
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kOutStaging = 4 * 2 * kStageTileBytes;  // 4 warps x 2 tiles
+  static constexpr int kBiasStaging = 4 * kEpiChunk * 4;       // 4 warps x 64 fp32
+  static constexpr int kSmemBytes =
+      kStages * kStageBytes + kOutStaging + kBiasStaging + 1024 /*align*/ + 256 /*barriers*/;
 };
-
-__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&v)[32], int valid) {
-  // valid: number of columns (multiple of 8) that are inside N.
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    if (q * 8 < valid) {
-      uint4 pk;
-      uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        __nv_bfloat162 h = __floats2bfloat162_rn(v[q * 8 + 2 * j], v[q * 8 + 2 * j + 1]);
-        w[j] = *reinterpret_cast<uint32_t*>(&h);
-      }
-      *reinterpret_cast<uint4*>(dst + q * 8) = pk;
-    }
-  }
-}
 
 __device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float (&v)[32], int valid) {
 #pragma unroll
@@ -111,16 +105,38 @@ __device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float (&v
   }
 }
 
+// Write 32 fp32 values (columns [half*32, half*32+32) of this lane's row) as
+// bf16 into a 128B-swizzled 32x64 staging tile (row = lane).
+__device__ __forceinline__ void stage_bf16x32(uint8_t* tile, int lane, int half, const float (&v)[32]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 pk;
+    uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(v[q * 8 + 2 * j], v[q * 8 + 2 * j + 1]);
+      w[j] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    const int chunk16 = half * 4 + q;  // 16-byte chunk within the 128-byte row
+    *reinterpret_cast<uint4*>(tile + lane * 128 + ((chunk16 ^ (lane & 7)) << 4)) = pk;
+  }
+}
+
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmAux,
+                     GemmParams p) {
   using Cfg = GemmCfg<BN>;
   constexpr int S = Cfg::kStages;
+  constexpr bool kF32Out = (EPI == kEpiPartialF32 || EPI == kEpiAccumF32);
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the 128B swizzle atoms.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stage_base = smem;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint8_t* out_stage = smem + S * Cfg::kStageBytes;  // [4 warps][2][32x64 bf16], 1024-aligned
+  float* bias_stage = reinterpret_cast<float*>(out_stage + Cfg::kOutStaging);  // [4 warps][64]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(out_stage + Cfg::kOutStaging + Cfg::kBiasStaging);
   uint64_t* full_bar = bars;               // [S]
   uint64_t* empty_bar = bars + S;          // [S]
   uint64_t* tfull_bar = bars + 2 * S;      // [2]
@@ -245,10 +261,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             phase ^= 1;
           }
         }
-        if (kb1 <= kb0) {
-          // Empty K range (cannot happen for valid shapes): still hand the
-          // (zero) accumulator over so the epilogue does not wait forever.
-        }
         umma_commit(&tfull_bar[acc]);
       }
     }
@@ -257,7 +269,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ------------------------------------------------------------ epilogue
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int row_in_tile = quad * 32 + lane;
+    uint8_t* my_stage = out_stage + (warp - 2) * 2 * kStageTileBytes;
+    float* my_bias = bias_stage + (warp - 2) * kEpiChunk;
     int iter = 0;
+    int chunk_count = 0;
     for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++iter) {
       const int tile = u % num_tiles;
       const int split = u / num_tiles;
@@ -275,82 +290,114 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int64_t tgt = -1;
       if (EPI == kEpiCEStats && row_ok) tgt = p.ce_targets[row] - p.ce_col0;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        float v[32];
-        tmem_ld32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN + c * 32, v);
-        tmem_wait_ld();
-        const int col = n0 + c * 32;
-        if (!row_ok || col >= p.N) continue;
-        const int valid = min(32, p.N - col);
-        if (EPI == kEpiPartialF32) {
-          float* dst = p.ws + (static_cast<size_t>(split) * p.M + row) * p.N + col;
-#pragma unroll
-          for (int q = 0; q < 8; ++q)
-            if (q * 4 < valid) *reinterpret_cast<float4*>(dst + q * 4) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-          continue;
+      for (int c = 0; c < BN / kEpiChunk; ++c) {
+        const int col0 = n0 + c * kEpiChunk;
+        if (col0 >= p.N) break;  // uniform across the CTA
+        if ((EPI == kEpiBias || EPI == kEpiBiasGelu || EPI == kEpiBiasResid) && p.bias != nullptr) {
+          const int bc = col0 + 2 * lane;
+          float2 bv = make_float2(0.f, 0.f);
+          if (bc < p.N) bv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p.bias + bc));
+          __syncwarp();
+          my_bias[2 * lane] = bv.x;
+          my_bias[2 * lane + 1] = bv.y;
+          __syncwarp();
         }
-        if (EPI == kEpiAccumF32) {
-          float* dst = p.ws + static_cast<size_t>(row) * p.N + col;
+        uint8_t* tile_a = my_stage + (chunk_count & 1) * kStageTileBytes;
+        uint8_t* tile_b = my_stage + ((chunk_count & 1) ^ 1) * kStageTileBytes;
+        if (!kF32Out) {
+          // The staging tile(s) about to be written must have been read by
+          // the TMA stores issued for earlier chunks.
+          if (lane == 0) {
+            if (EPI == kEpiBiasGelu)
+              bulk_wait_read<0>();
+            else
+              bulk_wait_read<1>();
+          }
+          __syncwarp();
+        }
 #pragma unroll
-          for (int q = 0; q < 8; ++q)
-            if (q * 4 < valid) {
-              float4 o = *reinterpret_cast<float4*>(dst + q * 4);
-              o.x += v[4 * q];
-              o.y += v[4 * q + 1];
-              o.z += v[4 * q + 2];
-              o.w += v[4 * q + 3];
-              *reinterpret_cast<float4*>(dst + q * 4) = o;
+        for (int half = 0; half < 2; ++half) {
+          const int col = col0 + half * 32;
+          float v[32];
+          tmem_ld32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN + c * kEpiChunk + half * 32, v);
+          tmem_wait_ld();
+          const int valid = max(0, min(32, p.N - col));
+          if (EPI == kEpiPartialF32 || EPI == kEpiAccumF32) {
+            if (!row_ok || valid == 0) continue;
+            float* dst = (EPI == kEpiPartialF32 ? p.ws + (static_cast<size_t>(split) * p.M + row) * p.N
+                                                : p.ws + static_cast<size_t>(row) * p.N) +
+                         col;
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              if (q * 4 < valid) {
+                float4 o = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                if (EPI == kEpiAccumF32) {
+                  const float4 old = *reinterpret_cast<float4*>(dst + q * 4);
+                  o.x += old.x;
+                  o.y += old.y;
+                  o.z += old.z;
+                  o.w += old.w;
+                }
+                *reinterpret_cast<float4*>(dst + q * 4) = o;
+              }
+            continue;
+          }
+          if (EPI == kEpiBias || EPI == kEpiBiasGelu || EPI == kEpiBiasResid) {
+            if (p.bias != nullptr) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] += my_bias[half * 32 + i];
             }
-          continue;
+          }
+          if (EPI == kEpiBiasGelu) {
+            stage_bf16x32(tile_b, lane, half, v);  // pre-activation
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              // gelu of the bf16-rounded pre-activation, so forward and the
+              // dGELU backward see the same input.
+              const float x = __bfloat162float(__float2bfloat16_rn(v[i]));
+              v[i] = gelu_tanh(x);
+            }
+          } else if (EPI == kEpiBiasResid) {
+            float r[32];
+            if (row_ok) load_bf16x32(p.aux + static_cast<size_t>(row) * p.ld_aux + col, r, valid);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] += row_ok ? r[i] : 0.f;
+          } else if (EPI == kEpiDGelu) {
+            float x[32];
+            if (row_ok) load_bf16x32(p.aux + static_cast<size_t>(row) * p.ld_aux + col, x, valid);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] *= row_ok ? gelu_tanh_grad(x[i]) : 0.f;
+          } else if (EPI == kEpiCEStats) {
+            float cm = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              v[i] = __bfloat162float(__float2bfloat16_rn(v[i]));
+              const int lc = col + i;  // local column
+              if (lc < p.ce_valid_cols) cm = fmaxf(cm, v[i]);
+              if (row_ok && lc == tgt) p.ce_tgt[row] = v[i];
+            }
+            if (cm > -INFINITY) {
+              const float nm = fmaxf(ce_m, cm);
+              float s = 0.f;
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (col + i < p.ce_valid_cols) s += __expf(v[i] - nm);
+              ce_s = ce_s * __expf(ce_m - nm) + s;
+              ce_m = nm;
+            }
+          }
+          stage_bf16x32(tile_a, lane, half, v);
         }
-        if (EPI == kEpiBias || EPI == kEpiBiasGelu || EPI == kEpiBiasResid) {
-          if (p.bias != nullptr) {
-            float b[32];
-            load_bf16x32(p.bias + col, b, valid);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] += b[i];
+        if (!kF32Out) {
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmOut, tile_a, col0, m0 + quad * 32);
+            if (EPI == kEpiBiasGelu) tma_store_2d(&tmAux, tile_b, col0, m0 + quad * 32);
+            bulk_commit();
           }
         }
-        __nv_bfloat16* out = p.out + static_cast<size_t>(row) * p.ldo + col;
-        if (EPI == kEpiBiasGelu) {
-          store_bf16x32(p.aux_out + static_cast<size_t>(row) * p.ldo + col, v, valid);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            // gelu of the bf16-rounded pre-activation, so forward and the
-            // dGELU backward see the same input.
-            float x = __bfloat162float(__float2bfloat16_rn(v[i]));
-            v[i] = gelu_tanh(x);
-          }
-        } else if (EPI == kEpiBiasResid) {
-          float r[32];
-          load_bf16x32(p.aux + static_cast<size_t>(row) * p.ld_aux + col, r, valid);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] += r[i];
-        } else if (EPI == kEpiDGelu) {
-          float x[32];
-          load_bf16x32(p.aux + static_cast<size_t>(row) * p.ld_aux + col, x, valid);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] *= gelu_tanh_grad(x[i]);
-        } else if (EPI == kEpiCEStats) {
-          float cm = -INFINITY;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            v[i] = __bfloat162float(__float2bfloat16_rn(v[i]));
-            const int lc = col + i;  // local column
-            if (lc < p.ce_valid_cols) cm = fmaxf(cm, v[i]);
-            if (lc == tgt) p.ce_tgt[row] = v[i];
-          }
-          if (cm > -INFINITY) {
-            const float nm = fmaxf(ce_m, cm);
-            float s = 0.f;
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (col + i < p.ce_valid_cols) s += __expf(v[i] - nm);
-            ce_s = ce_s * __expf(ce_m - nm) + s;
-            ce_m = nm;
-          }
-        }
-        store_bf16x32(out, v, valid);
+        ++chunk_count;
       }
       if (EPI == kEpiCEStats && row_ok) {
         const int n_tiles = num_n;
@@ -360,6 +407,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_before();
       mbar_arrive(&tempty_bar[acc]);
     }
+    if (!kF32Out && lane == 0) bulk_wait_all();
+    __syncwarp();
   }
 
   tc_fence_before();

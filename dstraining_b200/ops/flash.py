@@ -11,7 +11,11 @@ class _FlashFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, qkv, n_head, head_dim):
         qkv = qkv.contiguous()
-        out, lse = native.lib().flash_attn_fwd(qkv, n_head, head_dim)
+        lib = native.lib()
+        # tcgen05 kernel for 128-multiple sequence lengths, mma.sync tiles otherwise;
+        # both save the same base-2 log-sum-exp for the backward kernels.
+        fwd = lib.flash_attn_fwd_tc if qkv.shape[1] % 128 == 0 else lib.flash_attn_fwd
+        out, lse = fwd(qkv, n_head, head_dim)
         ctx.save_for_backward(qkv, out, lse)
         ctx.meta = (n_head, head_dim)
         return out

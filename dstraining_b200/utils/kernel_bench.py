@@ -1,0 +1,182 @@
+"""Per-kernel micro-benchmark for the native sm_100a kernels.
+
+    python -m dstraining_b200.utils.kernel_bench --suite gpt2        # every GPT-2-small shape
+    python -m dstraining_b200.utils.kernel_bench --op gemm --m 16384 --n 3072 --k 768 --layout nt --epi bias_gelu
+    python -m dstraining_b200.utils.kernel_bench --op attn --b 16 --t 1024 --h 12 --d 64 --dir bwd
+
+Each measurement: ``--warmup`` untimed calls, then ``--iters`` calls each
+timed alone with CUDA events on the launching stream, with a 256 MB buffer
+written between calls so L2 (126 MB) holds nothing useful; reports the mean
+time, achieved TFLOP/s (GEMM, attention) or GB/s (memory-bound kernels), and
+the fraction of the measured peaks in ``MEASURED_PEAKS.json`` (cuBLAS bf16
+burst and copy bandwidth) when that file exists. Used as the small, bounded
+case for ncu captures.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return d["bf16_tflops"], d["hbm_gbs"], "of measured"
+    return 1590.0, 6650.0, "of fallback"
+
+
+class Timer:
+    def __init__(self):
+        self.flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+
+    def run(self, fn, warmup, iters):
+        for _ in range(warmup):
+            fn()
+        total = 0.0
+        for _ in range(iters):
+            self.flush.fill_(1.0)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            s.record()
+            fn()
+            e.record()
+            torch.cuda.synchronize()
+            total += s.elapsed_time(e)
+        return total / iters
+
+
+def bf(*shape):
+    return torch.randn(*shape, device="cuda").to(torch.bfloat16)
+
+
+def bench_gemm(t, m, n, k, layout, epi, warmup, iters):
+    from dstraining_b200.ops import gemm as G
+
+    a_mn, b_mn = {"nt": (False, False), "nn": (False, True), "tn": (True, True)}[layout]
+    A = bf(k, m) if a_mn else bf(m, k)
+    B = bf(k, n) if b_mn else bf(n, k)
+    bias, aux, aux_out = bf(n), bf(m, n), torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    code = {"store": G.EPI_STORE, "bias": G.EPI_BIAS, "bias_gelu": G.EPI_BIAS_GELU, "bias_resid": G.EPI_BIAS_RESID, "splitk": -1,
+            "dgelu": G.EPI_DGELU}[epi]
+    if epi == "splitk":
+        fn = lambda: G.weight_grad(A, B)  # noqa: E731
+    else:
+        fn = lambda: G.gemm(A, a_mn, B, b_mn, code, bias=bias if "bias" in epi else None,  # noqa: E731
+                            aux=aux if epi in ("bias_resid", "dgelu") else None,
+                            aux_out=aux_out if epi == "bias_gelu" else None)
+    ms = t.run(fn, warmup, iters)
+    return ms, 2.0 * m * n * k / (ms * 1e-3) / 1e12
+
+
+def bench_attn(t, b, tl, h, d, direction, warmup, iters):
+    from dstraining_b200.ops import native
+
+    lib = native.lib()
+    qkv = bf(b, tl, 3 * h * d)
+    fwd = lib.flash_attn_fwd_tc if tl % 128 == 0 else lib.flash_attn_fwd  # the model's dispatch
+    out, lse = fwd(qkv, h, d)
+    dout = bf(b, tl, h * d)
+    if direction == "fwd":
+        fn = lambda: fwd(qkv, h, d)  # noqa: E731
+        flops = 4.0 * b * h * tl * tl * d / 2
+    else:
+        fn = lambda: lib.flash_attn_bwd(dout, qkv, out, lse, h, d)  # noqa: E731
+        flops = 10.0 * b * h * tl * tl * d / 2  # dV, dK, dQ, dP + the recomputed S
+    ms = t.run(fn, warmup, iters)
+    return ms, flops / (ms * 1e-3) / 1e12
+
+
+def bench_ln(t, rows, c, direction, warmup, iters):
+    from dstraining_b200.ops import native
+
+    lib = native.lib()
+    x, w, b, dy = bf(rows, c), bf(c), bf(c), bf(rows, c)
+    y, mean, rstd = lib.layernorm_fwd(x, w, b, 1e-5)
+    if direction == "fwd":
+        fn = lambda: lib.layernorm_fwd(x, w, b, 1e-5)  # noqa: E731
+        nbytes = 2 * rows * c * 2
+    else:
+        fn = lambda: lib.layernorm_bwd(dy, x, w, mean, rstd)  # noqa: E731
+        nbytes = 3 * rows * c * 2 + 2 * rows * c * 2  # dx pass + the dγ/dβ column pass
+    ms = t.run(fn, warmup, iters)
+    return ms, nbytes / (ms * 1e-3) / 1e9
+
+
+def gpt2_suite(t, warmup, iters):
+    tok, C, V = 16384, 768, 50304
+    rows = []
+    for name, (m, n, k, lay, epi) in {
+        "qkv fwd": (tok, 3 * C, C, "nt", "bias"),
+        "proj fwd (+resid)": (tok, C, C, "nt", "bias_resid"),
+        "fc fwd (+gelu)": (tok, 4 * C, C, "nt", "bias_gelu"),
+        "c_proj fwd (+resid)": (tok, C, 4 * C, "nt", "bias_resid"),
+        "head fwd": (tok, V, C, "nt", "store"),
+        "c_proj dX (+dgelu)": (tok, 4 * C, C, "nn", "dgelu"),
+        "fc dX": (tok, C, 4 * C, "nn", "store"),
+        "qkv dX": (tok, C, 3 * C, "nn", "store"),
+        "head dX": (tok, C, V, "nn", "store"),
+        "fc dW (split-K)": (4 * C, C, tok, "tn", "splitk"),
+        "c_proj dW (split-K)": (C, 4 * C, tok, "tn", "splitk"),
+        "qkv dW (split-K)": (3 * C, C, tok, "tn", "splitk"),
+        "head dW": (V, C, tok, "tn", "store"),
+    }.items():
+        ms, tf = bench_gemm(t, m, n, k, lay, epi, warmup, iters)
+        rows.append((name, f"{m}x{n}x{k}", ms, tf, "TFLOP/s"))
+    for d in ("fwd", "bwd"):
+        ms, tf = bench_attn(t, 16, 1024, 12, 64, d, warmup, iters)
+        rows.append((f"attention {d}", "b16 t1024 h12 d64", ms, tf, "TFLOP/s"))
+    for d in ("fwd", "bwd"):
+        ms, gb = bench_ln(t, tok, C, d, warmup, iters)
+        rows.append((f"layernorm {d}", f"{tok}x{C}", ms, gb, "GB/s"))
+    return rows
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--suite", choices=["gpt2"], default=None)
+    ap.add_argument("--op", choices=["gemm", "attn", "ln"], default="gemm")
+    ap.add_argument("--m", type=int, default=16384)
+    ap.add_argument("--n", type=int, default=3072)
+    ap.add_argument("--k", type=int, default=768)
+    ap.add_argument("--layout", default="nt")
+    ap.add_argument("--epi", default="store")
+    ap.add_argument("--b", type=int, default=16)
+    ap.add_argument("--t", type=int, default=1024)
+    ap.add_argument("--h", type=int, default=12)
+    ap.add_argument("--d", type=int, default=64)
+    ap.add_argument("--rows", type=int, default=16384)
+    ap.add_argument("--c", type=int, default=768)
+    ap.add_argument("--dir", default="fwd")
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--iters", type=int, default=10)
+    a = ap.parse_args()
+    torch.cuda.set_device(0)
+    t = Timer()
+    tf_peak, gb_peak, tag = peaks()
+    if a.suite == "gpt2":
+        rows = gpt2_suite(t, a.warmup, a.iters)
+    elif a.op == "gemm":
+        ms, tf = bench_gemm(t, a.m, a.n, a.k, a.layout, a.epi, a.warmup, a.iters)
+        rows = [(f"gemm {a.layout} {a.epi}", f"{a.m}x{a.n}x{a.k}", ms, tf, "TFLOP/s")]
+    elif a.op == "attn":
+        ms, tf = bench_attn(t, a.b, a.t, a.h, a.d, a.dir, a.warmup, a.iters)
+        rows = [(f"attention {a.dir}", f"b{a.b} t{a.t} h{a.h} d{a.d}", ms, tf, "TFLOP/s")]
+    else:
+        ms, gb = bench_ln(t, a.rows, a.c, a.dir, a.warmup, a.iters)
+        rows = [(f"layernorm {a.dir}", f"{a.rows}x{a.c}", ms, gb, "GB/s")]
+    print(f"{'kernel':24s} {'shape':22s} {'ms':>8s} {'achieved':>10s}  fraction")
+    for name, shape, ms, val, unit in rows:
+        peak = tf_peak if unit == "TFLOP/s" else gb_peak
+        print(f"{name:24s} {shape:22s} {ms:8.4f} {val:8.1f} {unit:7s} {val / peak:6.1%} {tag}")
+
+
+if __name__ == "__main__":
+    main()

@@ -203,3 +203,17 @@ def test_adam_matches_torch():
         assert torch.equal(p.data, m.to(torch.bfloat16))
     st = opt.inner.state[opt.master_params[0]]
     assert st["exp_avg"].dtype == torch.float32 and float(st["step"]) == 3
+
+
+@pytest.mark.parametrize("B,T,H,D", [(2, 128, 4, 64), (1, 512, 3, 128), (2, 1024, 12, 64), (1, 2048, 2, 128)])
+def test_flash_forward_tcgen05(B, T, H, D):
+    """The tcgen05 forward matches the fp32 reference and the mma.sync
+    forward, including the saved log-sum-exp that backward consumes."""
+    lib = _lib()
+    qkv = _bf(B, T, 3 * H * D, seed=30)
+    out, lse = lib.flash_attn_fwd_tc(qkv, H, D)
+    ref = _ref_attention(qkv, H, D)
+    assert _rel(out, ref) < 2e-2
+    out2, lse2 = lib.flash_attn_fwd(qkv, H, D)
+    assert (lse - lse2).abs().max().item() < 2e-2
+    assert _rel(out, out2) < 2e-2
