@@ -334,6 +334,422 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+
+// ------------------------------------------------------------------ backward
+// Di[b, h, t] = sum_d dO[b, t, h, d] * O[b, t, h, d]; one warp per (b, t, h).
+__global__ void bwd_rowdot_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ out,
+                                  float* __restrict__ di, int rows, int T, int H, int D) {
+  const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (w >= rows) return;
+  const __nv_bfloat16* a = dout + static_cast<size_t>(w) * D;
+  const __nv_bfloat16* c = out + static_cast<size_t>(w) * D;
+  float acc = 0.f;
+  for (int d = lane * 2; d < D; d += 64) {
+    const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(a + d));
+    const float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(c + d));
+    acc += x.x * y.x + x.y * y.y;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffff, acc, o);
+  if (lane == 0) {
+    const int hh = w % H, bt = w / H;
+    di[(static_cast<size_t>(bt / T) * H + hh) * T + bt % T] = acc;
+  }
+}
+
+__device__ __forceinline__ void store_row_bf16(__nv_bfloat16* dst, const float (&v)[32], float scale) {
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    uint4 pk;
+    uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      __nv_bfloat162 hv = __floats2bfloat162_rn(v[i + 2 * t] * scale, v[i + 2 * t + 1] * scale);
+      w[t] = *reinterpret_cast<uint32_t*>(&hv);
+    }
+    *reinterpret_cast<uint4*>(dst + i) = pk;
+  }
+}
+
+// dK / dV: one CTA per (128-key block, head, batch), walking the query blocks
+// (BQ rows) at or after the key block. Per query block:
+//   S^T = K Q^T, dP^T = V dO^T            (tcgen05, M=128 keys, N=BQ)
+//   P^T = exp2(S^T * scale - lse2[q]), dS^T = P^T * (dP^T - Di[q])   (8 warps)
+//   dV += P^T dO, dK += dS^T Q            (tcgen05, M=128, N=D, TMEM-resident)
+template <int D, int BQ>
+struct DkdvCfg {
+  static constexpr int kDAtoms = D / 64;
+  static constexpr int kKVTile = kDAtoms * kAtom;  // 128 rows x D
+  static constexpr int kQAtom = BQ * 128;          // BQ rows x 64 columns
+  static constexpr int kQTile = kDAtoms * kQAtom;
+  static constexpr int kPTile = (BQ / 64) * kAtom;  // 128 rows x BQ
+  static constexpr int kSmem = 2 * kKVTile + 4 * kQTile + 2 * kPTile + 4 * BQ * 4 + 1024 + 256;
+};
+
+template <int D, int BQ>
+__global__ void __launch_bounds__(kThreads, 1)
+    dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmKV, const __grid_constant__ CUtensorMap tmQ,
+                   const __grid_constant__ CUtensorMap tmDO, const float* __restrict__ lse2,
+                   const float* __restrict__ di, __nv_bfloat16* __restrict__ dqkv, int T, int H, float scale_log2,
+                   float scale, int* status) {
+  using C = DkdvCfg<D, BQ>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + C::kKVTile;
+  uint8_t* sQ = sV + C::kKVTile;     // [2][kQTile]
+  uint8_t* sDO = sQ + 2 * C::kQTile; // [2][kQTile]
+  uint8_t* sP = sDO + 2 * C::kQTile;
+  uint8_t* sDS = sP + C::kPTile;
+  float* sL = reinterpret_cast<float*>(sDS + C::kPTile);  // [2][BQ]
+  float* sDi = sL + 2 * BQ;                               // [2][BQ]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDi + 2 * BQ);
+  uint64_t* kv_full = bars;
+  uint64_t* q_full = bars + 1;   // [2]
+  uint64_t* q_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;
+  uint64_t* s_free = bars + 6;
+  uint64_t* p_full = bars + 7;
+  uint64_t* pd_free = bars + 8;
+  uint64_t* fin = bars + 9;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+
+  const int kb = blockIdx.x;  // key block 0 has the most query blocks: first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = b * T, k0 = kb * BM;
+  const int qb0 = k0 / BQ;
+  const int nq = T / BQ - qb0;
+  const float* lrow = lse2 + (static_cast<size_t>(b) * H + h) * T;
+  const float* drow = di + (static_cast<size_t>(b) * H + h) * T;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 256);
+    mbar_init(p_full, 256);
+    mbar_init(pd_free, 1);
+    mbar_init(fin, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tDP = tmem + BQ, tDV = tmem + 2 * BQ, tDK = tmem + 2 * BQ + D;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      mbar_arrive_expect_tx(kv_full, 2 * C::kKVTile);
+#pragma unroll
+      for (int a = 0; a < C::kDAtoms; ++a) {
+        tma_load_2d(sK + a * kAtom, &tmKV, kv_full, h * 3 * D + D + a * 64, row0 + k0);
+        tma_load_2d(sV + a * kAtom, &tmKV, kv_full, h * 3 * D + 2 * D + a * 64, row0 + k0);
+      }
+      for (int i = 0; i < nq; ++i) {
+        const int st = i & 1;
+        if (!mbar_wait(&q_empty[st], ((i >> 1) & 1) ^ 1, status, kTimeoutSmemEmpty)) break;
+        const int q0 = (qb0 + i) * BQ;
+        mbar_arrive_expect_tx(&q_full[st], 2 * C::kQTile + 2 * BQ * 4);
+#pragma unroll
+        for (int a = 0; a < C::kDAtoms; ++a) {
+          tma_load_2d(sQ + st * C::kQTile + a * C::kQAtom, &tmQ, &q_full[st], h * 3 * D + a * 64, row0 + q0);
+          tma_load_2d(sDO + st * C::kQTile + a * C::kQAtom, &tmDO, &q_full[st], h * D + a * 64, row0 + q0);
+        }
+        bulk_load(sL + st * BQ, lrow + q0, BQ * 4, &q_full[st]);
+        bulk_load(sDi + st * BQ, drow + q0, BQ * 4, &q_full[st]);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idS = idesc_bf16_f32(BM, BQ, false, false);
+      constexpr uint32_t idG = idesc_bf16_f32(BM, D, false, true);
+      bool ok = mbar_wait(kv_full, 0, status, kTimeoutTmaFull);
+      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV), p_addr = smem_u32(sP), ds_addr = smem_u32(sDS);
+      for (int i = 0; i < nq && ok; ++i) {
+        const int st = i & 1;
+        const uint32_t ph = (i >> 1) & 1, pi = i & 1;
+        ok = mbar_wait(&q_full[st], ph, status, kTimeoutTmaFull) && mbar_wait(s_free, pi ^ 1, status, kTimeoutTmemEmpty);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t q_addr = smem_u32(sQ + st * C::kQTile), do_addr = smem_u32(sDO + st * C::kQTile);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t a_off = (kk >> 2) * kAtom + (kk & 3) * 32;
+          const uint32_t b_off = (kk >> 2) * C::kQAtom + (kk & 3) * 32;
+          umma_f16_ss(tS, smem_desc_sw128(k_addr + a_off, 16, 1024), smem_desc_sw128(q_addr + b_off, 16, 1024), idS,
+                      kk > 0 ? 1u : 0u);
+          umma_f16_ss(tDP, smem_desc_sw128(v_addr + a_off, 16, 1024), smem_desc_sw128(do_addr + b_off, 16, 1024), idS,
+                      kk > 0 ? 1u : 0u);
+        }
+        umma_commit(s_full);
+        if (!(ok = mbar_wait(p_full, pi, status, kTimeoutTmaFull))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BQ / 16; ++kk) {
+          const uint32_t a_off = (kk >> 2) * kAtom + (kk & 3) * 32;
+          const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+          umma_f16_ss(tDV, smem_desc_sw128(p_addr + a_off, 16, 1024), smem_desc_sw128(do_addr + kk * 2048, C::kQAtom, 1024),
+                      idG, acc);
+          umma_f16_ss(tDK, smem_desc_sw128(ds_addr + a_off, 16, 1024), smem_desc_sw128(q_addr + kk * 2048, C::kQAtom, 1024),
+                      idG, acc);
+        }
+        umma_commit(&q_empty[st]);
+        umma_commit(pd_free);
+      }
+      umma_commit(fin);
+    }
+    __syncwarp();
+  } else {
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int r = quad * 32 + lane;
+    const int key = k0 + r;
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    constexpr int HB = BQ / 2;  // query columns per thread
+    bool ok = true;
+    for (int i = 0; i < nq && ok; ++i) {
+      const int st = i & 1;
+      const uint32_t ph = (i >> 1) & 1, pi = i & 1;
+      ok = mbar_wait(&q_full[st], ph, status, kTimeoutTmaFull) && mbar_wait(s_full, pi, status, kTimeoutTmemFull) &&
+           mbar_wait(pd_free, pi ^ 1, status, kTimeoutTmemFull);
+      if (!ok) break;
+      tc_fence_after();
+      const int q0 = (qb0 + i) * BQ;
+#pragma unroll
+      for (int c = 0; c < HB / 32; ++c) {
+        const int col = half * HB + c * 32;
+        float sv[32], dp[32];
+        tmem_ld32(tS + col + lane_off, sv);
+        tmem_ld32(tDP + col + lane_off, dp);
+        tmem_wait_ld();
+#pragma unroll
+        for (int t = 0; t < 32; ++t) {
+          const int qc = col + t;
+          const float p = (key > q0 + qc) ? 0.f : exp2f(sv[t] * scale_log2 - sL[st * BQ + qc]);
+          sv[t] = p;
+          dp[t] = p * (dp[t] - sDi[st * BQ + qc]);
+        }
+        store_p_quarter(sP, r, col / 32, sv);
+        store_p_quarter(sDS, r, col / 32, dp);
+      }
+      tc_fence_before();
+      mbar_arrive(s_free);
+      fence_proxy_async_smem();
+      mbar_arrive(p_full);
+    }
+    if (ok && mbar_wait(fin, 0, status, kTimeoutTmemFull)) {
+      tc_fence_after();
+      __nv_bfloat16* krow = dqkv + (static_cast<size_t>(row0 + key) * H + h) * 3 * D + D + half * (D / 2);
+      __nv_bfloat16* vrow = krow + D;
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        float v[32];
+        tmem_ld32(tDK + half * (D / 2) + c * 32 + lane_off, v);
+        tmem_wait_ld();
+        store_row_bf16(krow + c * 32, v, scale);
+        tmem_ld32(tDV + half * (D / 2) + c * 32 + lane_off, v);
+        tmem_wait_ld();
+        store_row_bf16(vrow + c * 32, v, 1.f);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// dQ: one CTA per (128-query block, head, batch), walking key blocks (BK
+// wide) up to the diagonal:
+//   S = Q K^T, dP = dO V^T                 (tcgen05, M=128 queries, N=BK)
+//   dS = exp2(S * scale - lse2) * (dP - Di)   (8 warps, into shared memory)
+//   dQ += dS K                             (tcgen05, M=128, N=D, TMEM-resident)
+template <int D, int BK>
+struct DqCfg {
+  static constexpr int kDAtoms = D / 64;
+  static constexpr int kQTile = kDAtoms * kAtom;  // 128 rows x D
+  static constexpr int kKAtom = BK * 128;
+  static constexpr int kKTile = kDAtoms * kKAtom;  // BK rows x D
+  static constexpr int kSTile = (BK / 64) * kAtom;  // 128 rows x BK
+  static constexpr int kSmem = 2 * kQTile + 4 * kKTile + kSTile + 1024 + 256;
+};
+
+template <int D, int BK>
+__global__ void __launch_bounds__(kThreads, 1)
+    dq_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
+                 const __grid_constant__ CUtensorMap tmKV, const float* __restrict__ lse2, const float* __restrict__ di,
+                 __nv_bfloat16* __restrict__ dqkv, int T, int H, float scale_log2, float scale, int* status) {
+  using C = DqCfg<D, BK>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sDO = sQ + C::kQTile;
+  uint8_t* sK = sDO + C::kQTile;     // [2][kKTile]
+  uint8_t* sV = sK + 2 * C::kKTile;  // [2][kKTile]
+  uint8_t* sDS = sV + 2 * C::kKTile;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDS + C::kSTile);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;
+  uint64_t* s_free = bars + 6;
+  uint64_t* p_full = bars + 7;
+  uint64_t* pd_free = bars + 8;
+  uint64_t* fin = bars + 9;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+
+  const int qb = gridDim.x - 1 - blockIdx.x;  // heaviest (most key blocks) first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = b * T, q0 = qb * BM;
+  const int nkb = (q0 + BM - 1) / BK + 1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 256);
+    mbar_init(p_full, 256);
+    mbar_init(pd_free, 1);
+    mbar_init(fin, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tDP = tmem + BK, tDQ = tmem + 2 * BK;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      mbar_arrive_expect_tx(q_full, 2 * C::kQTile);
+#pragma unroll
+      for (int a = 0; a < C::kDAtoms; ++a) {
+        tma_load_2d(sQ + a * kAtom, &tmQ, q_full, h * 3 * D + a * 64, row0 + q0);
+        tma_load_2d(sDO + a * kAtom, &tmDO, q_full, h * D + a * 64, row0 + q0);
+      }
+      for (int j = 0; j < nkb; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, status, kTimeoutSmemEmpty)) break;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * C::kKTile);
+#pragma unroll
+        for (int a = 0; a < C::kDAtoms; ++a) {
+          tma_load_2d(sK + st * C::kKTile + a * C::kKAtom, &tmKV, &kv_full[st], h * 3 * D + D + a * 64, row0 + j * BK);
+          tma_load_2d(sV + st * C::kKTile + a * C::kKAtom, &tmKV, &kv_full[st], h * 3 * D + 2 * D + a * 64, row0 + j * BK);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idS = idesc_bf16_f32(BM, BK, false, false);
+      constexpr uint32_t idG = idesc_bf16_f32(BM, D, false, true);
+      bool ok = mbar_wait(q_full, 0, status, kTimeoutTmaFull);
+      const uint32_t q_addr = smem_u32(sQ), do_addr = smem_u32(sDO), ds_addr = smem_u32(sDS);
+      for (int j = 0; j < nkb && ok; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1, pj = j & 1;
+        ok = mbar_wait(&kv_full[st], ph, status, kTimeoutTmaFull) && mbar_wait(s_free, pj ^ 1, status, kTimeoutTmemEmpty);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(sK + st * C::kKTile), v_addr = smem_u32(sV + st * C::kKTile);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t a_off = (kk >> 2) * kAtom + (kk & 3) * 32;
+          const uint32_t b_off = (kk >> 2) * C::kKAtom + (kk & 3) * 32;
+          umma_f16_ss(tS, smem_desc_sw128(q_addr + a_off, 16, 1024), smem_desc_sw128(k_addr + b_off, 16, 1024), idS,
+                      kk > 0 ? 1u : 0u);
+          umma_f16_ss(tDP, smem_desc_sw128(do_addr + a_off, 16, 1024), smem_desc_sw128(v_addr + b_off, 16, 1024), idS,
+                      kk > 0 ? 1u : 0u);
+        }
+        umma_commit(s_full);
+        if (!(ok = mbar_wait(p_full, pj, status, kTimeoutTmaFull))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          const uint32_t a_off = (kk >> 2) * kAtom + (kk & 3) * 32;
+          umma_f16_ss(tDQ, smem_desc_sw128(ds_addr + a_off, 16, 1024), smem_desc_sw128(k_addr + kk * 2048, C::kKAtom, 1024),
+                      idG, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&kv_empty[st]);
+        umma_commit(pd_free);
+      }
+      umma_commit(fin);
+    }
+    __syncwarp();
+  } else {
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int r = quad * 32 + lane;
+    const int q = q0 + r;
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    const float lq = lse2[(static_cast<size_t>(b) * H + h) * T + q];
+    const float dq_i = di[(static_cast<size_t>(b) * H + h) * T + q];
+    constexpr int HB = BK / 2;
+    bool ok = true;
+    for (int j = 0; j < nkb && ok; ++j) {
+      const uint32_t pj = j & 1;
+      ok = mbar_wait(s_full, pj, status, kTimeoutTmemFull) && mbar_wait(pd_free, pj ^ 1, status, kTimeoutTmemFull);
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < HB / 32; ++c) {
+        const int col = half * HB + c * 32;
+        float sv[32], dp[32];
+        tmem_ld32(tS + col + lane_off, sv);
+        tmem_ld32(tDP + col + lane_off, dp);
+        tmem_wait_ld();
+#pragma unroll
+        for (int t = 0; t < 32; ++t) {
+          const int kk = j * BK + col + t;
+          const float p = (kk > q) ? 0.f : exp2f(sv[t] * scale_log2 - lq);
+          dp[t] = p * (dp[t] - dq_i);
+        }
+        store_p_quarter(sDS, r, col / 32, dp);
+      }
+      tc_fence_before();
+      mbar_arrive(s_free);
+      fence_proxy_async_smem();
+      mbar_arrive(p_full);
+    }
+    if (ok && mbar_wait(fin, 0, status, kTimeoutTmemFull)) {
+      tc_fence_after();
+      __nv_bfloat16* qrow = dqkv + (static_cast<size_t>(row0 + q) * H + h) * 3 * D + half * (D / 2);
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        float v[32];
+        tmem_ld32(tDQ + half * (D / 2) + c * 32 + lane_off, v);
+        tmem_wait_ld();
+        store_row_bf16(qrow + c * 32, v, scale);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 }  // namespace attn_tc
 }  // namespace dst
 
@@ -369,6 +785,64 @@ std::vector<at::Tensor> flash_attn_fwd_tc(const at::Tensor& qkv, int64_t H, int6
   return {out, lse};
 }
 
+
+// Backward on the tensor-core path; T must be a multiple of 128.
+at::Tensor flash_attn_bwd_tc(const at::Tensor& dout, const at::Tensor& qkv, const at::Tensor& out,
+                             const at::Tensor& lse, int64_t H, int64_t D) {
+  TORCH_CHECK(qkv.is_cuda() && qkv.scalar_type() == at::kBFloat16 && qkv.dim() == 3 && qkv.is_contiguous(),
+              "attention bwd: contiguous bf16 qkv required");
+  TORCH_CHECK(D == 64 || D == 128, "attention: head_dim must be 64 or 128");
+  TORCH_CHECK(qkv.size(2) == 3 * H * D && qkv.size(1) % 128 == 0, "attention bwd (tc): shapes");
+  TORCH_CHECK(dout.is_contiguous() && out.is_contiguous() && dout.sizes() == out.sizes(), "attention bwd: dout/out");
+  TORCH_CHECK(lse.is_contiguous() && lse.scalar_type() == at::kFloat, "attention bwd: lse");
+  c10::cuda::CUDAGuard g(qkv.device());
+  const int B = qkv.size(0), T = qkv.size(1);
+  at::Tensor dqkv = at::empty_like(qkv);
+  at::Tensor di = at::empty({B, H, T}, qkv.options().dtype(at::kFloat));
+  const double sc = 1.0 / std::sqrt(static_cast<double>(D));
+  const float scale = static_cast<float>(sc), scale_log2 = static_cast<float>(sc * 1.4426950408889634);
+  auto st = at::cuda::getCurrentCUDAStream();
+  const int rows = B * T * static_cast<int>(H);
+  attn_tc::bwd_rowdot_kernel<<<(rows + 7) / 8, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
+                                                             reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()),
+                                                             di.data_ptr<float>(), rows, T, H, D);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  const uint64_t nrows = static_cast<uint64_t>(B) * T;
+  const int blk = (D == 64) ? 128 : 64;  // inner block: BQ of dK/dV, BK of dQ
+  CUtensorMap tmQKV128 = make_tmap_bf16(qkv.data_ptr(), 3 * H * D, nrows, 3 * H * D, 64, 128);
+  CUtensorMap tmQKVb = make_tmap_bf16(qkv.data_ptr(), 3 * H * D, nrows, 3 * H * D, 64, blk);
+  CUtensorMap tmDO128 = make_tmap_bf16(dout.data_ptr(), H * D, nrows, H * D, 64, 128);
+  CUtensorMap tmDOb = make_tmap_bf16(dout.data_ptr(), H * D, nrows, H * D, 64, blk);
+  auto* dq = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
+  const float* l = lse.data_ptr<float>();
+  const float* d = di.data_ptr<float>();
+  dim3 grid(T / 128, H, B);
+  if (D == 64) {
+    auto k1 = attn_tc::dkdv_tc_kernel<64, 128>;
+    constexpr int s1 = attn_tc::DkdvCfg<64, 128>::kSmem;
+    C10_CUDA_CHECK(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, s1));
+    k1<<<grid, attn_tc::kThreads, s1, st>>>(tmQKV128, tmQKVb, tmDOb, l, d, dq, T, H, scale_log2, scale, status_ptr());
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    auto k2 = attn_tc::dq_tc_kernel<64, 128>;
+    constexpr int s2 = attn_tc::DqCfg<64, 128>::kSmem;
+    C10_CUDA_CHECK(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, s2));
+    k2<<<grid, attn_tc::kThreads, s2, st>>>(tmQKV128, tmDO128, tmQKVb, l, d, dq, T, H, scale_log2, scale, status_ptr());
+  } else {
+    auto k1 = attn_tc::dkdv_tc_kernel<128, 64>;
+    constexpr int s1 = attn_tc::DkdvCfg<128, 64>::kSmem;
+    C10_CUDA_CHECK(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, s1));
+    k1<<<grid, attn_tc::kThreads, s1, st>>>(tmQKV128, tmQKVb, tmDOb, l, d, dq, T, H, scale_log2, scale, status_ptr());
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    auto k2 = attn_tc::dq_tc_kernel<128, 64>;
+    constexpr int s2 = attn_tc::DqCfg<128, 64>::kSmem;
+    C10_CUDA_CHECK(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, s2));
+    k2<<<grid, attn_tc::kThreads, s2, st>>>(tmQKV128, tmDO128, tmQKVb, l, d, dq, T, H, scale_log2, scale, status_ptr());
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return dqkv;
+}
+
 void register_attn_tc(pybind11::module& m) {
   m.def("flash_attn_fwd_tc", &flash_attn_fwd_tc, "causal flash attention forward on tcgen05 (T % 128 == 0)");
+  m.def("flash_attn_bwd_tc", &flash_attn_bwd_tc, "causal flash attention backward on tcgen05 (T % 128 == 0)");
 }

@@ -24,7 +24,9 @@ class _FlashFn(torch.autograd.Function):
     def backward(ctx, dout):
         qkv, out, lse = ctx.saved_tensors
         n_head, head_dim = ctx.meta
-        dqkv = native.lib().flash_attn_bwd(dout.contiguous(), qkv, out, lse, n_head, head_dim)
+        lib = native.lib()
+        bwd = lib.flash_attn_bwd_tc if qkv.shape[1] % 128 == 0 else lib.flash_attn_bwd
+        dqkv = bwd(dout.contiguous(), qkv, out, lse, n_head, head_dim)
         return dqkv, None, None
 
 

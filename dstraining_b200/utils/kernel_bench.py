@@ -88,7 +88,8 @@ def bench_attn(t, b, tl, h, d, direction, warmup, iters):
         fn = lambda: fwd(qkv, h, d)  # noqa: E731
         flops = 4.0 * b * h * tl * tl * d / 2
     else:
-        fn = lambda: lib.flash_attn_bwd(dout, qkv, out, lse, h, d)  # noqa: E731
+        bwd = lib.flash_attn_bwd_tc if tl % 128 == 0 else lib.flash_attn_bwd
+        fn = lambda: bwd(dout, qkv, out, lse, h, d)  # noqa: E731
         flops = 10.0 * b * h * tl * tl * d / 2  # dV, dK, dQ, dP + the recomputed S
     ms = t.run(fn, warmup, iters)
     return ms, flops / (ms * 1e-3) / 1e12

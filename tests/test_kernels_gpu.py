@@ -217,3 +217,22 @@ def test_flash_forward_tcgen05(B, T, H, D):
     out2, lse2 = lib.flash_attn_fwd(qkv, H, D)
     assert (lse - lse2).abs().max().item() < 2e-2
     assert _rel(out, out2) < 2e-2
+
+
+@pytest.mark.parametrize("B,T,H,D", [(2, 128, 4, 64), (1, 512, 3, 128), (2, 1024, 12, 64), (1, 2048, 2, 128)])
+def test_flash_backward_tcgen05(B, T, H, D):
+    """tcgen05 backward vs the fp32 reference and the mma.sync backward;
+    bitwise deterministic across runs."""
+    lib = _lib()
+    qkv = _bf(B, T, 3 * H * D, seed=40)
+    dout = _bf(B, T, H * D, seed=41)
+    out, lse = lib.flash_attn_fwd_tc(qkv, H, D)
+    g = lib.flash_attn_bwd_tc(dout, qkv, out, lse, H, D)
+    g_old = lib.flash_attn_bwd(dout, qkv, out, lse, H, D)
+    qr = qkv.float().requires_grad_(True)
+    _ref_attention(qr, H, D).backward(dout.float())
+    gv, gr, go = g.float().view(B, T, H, 3, D), qr.grad.view(B, T, H, 3, D), g_old.float().view(B, T, H, 3, D)
+    for i, name in enumerate("qkv"):
+        assert _rel(gv[..., i, :], gr[..., i, :]) < 3e-2, name
+        assert _rel(gv[..., i, :], go[..., i, :]) < 3e-2, name
+    assert torch.equal(g, lib.flash_attn_bwd_tc(dout, qkv, out, lse, H, D))
