@@ -44,4 +44,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_ce(m);
   register_attn(m);
   register_attn_tc(m);
+  register_symm(m);
 }

@@ -100,7 +100,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// 2-D tiled bulk tensor load global -> shared (no multicast), completing on
+// 2-D tiled bulk tensor load global -> shared (this CTA only), completing on
 // the mbarrier's transaction count. Coordinates: c0 innermost.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
   asm volatile(
@@ -110,7 +110,7 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
-// Untiled bulk copy global -> shared (no multicast), completing on the
+// Untiled bulk copy global -> shared (this CTA only), completing on the
 // mbarrier's transaction count. Both addresses 16-byte aligned, size a
 // multiple of 16.
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {

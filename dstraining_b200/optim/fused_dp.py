@@ -1,0 +1,257 @@
+"""Data-parallel gradient reduction fused with the fp32-master Adam update.
+
+``FusedDPAdam(model, dp, lr=..., betas=..., eps=...)`` replaces the pair
+``GradReducer`` + ``MasterWeightOptimizer`` for bf16 models on CUDA. Parameters
+are packed into ~25 MiB buckets in reverse registration order (roughly the
+order backward finishes them). Each bucket owns two peer buffers
+(:class:`dstraining_b200.parallel.symm.PeerBuffer`), one for its gradients and
+one for its parameters; every parameter's ``.data`` becomes a view of the
+parameter buffer. As backward finishes a bucket (post-accumulate-grad hooks
+copy the gradients into its gradient buffer), the bucket's fused kernel is
+launched on a side stream:
+
+  each rank sums its 1/N slice of the bucket from all ranks' gradient buffers
+  over NVLink (fixed rank order), scales by 1/N, applies Adam to its fp32
+  master / moment slices, and stores the bf16 result into every rank's
+  parameter buffer - reduce-scatter, optimizer and all-gather in one launch.
+
+Adam state is therefore sharded (ZeRO-1: 1/N of the masters and moments per
+rank) and the optimizer work per GPU shrinks with N. ``step()`` launches the
+buckets that are still pending (all of them for pipeline schedules, which call
+it after ``train_step``; the bucket of sequence-parallel partial-gradient
+parameters always waits for ``finalize_grads``) and makes the compute stream
+wait for the side stream. Buckets launch strictly in bucket order so every
+rank issues the same kernel sequence.
+
+Without CUDA (gloo) the same bookkeeping runs with the collective and the
+update done by PyTorch ops (all-reduce, Adam on the owned slice, all-gather):
+the CPU correctness path. The update matches ``torch.optim.Adam``.
+"""
+
+from __future__ import annotations
+
+from typing import List, Optional
+
+import torch
+import torch.distributed as dist
+
+from ..ops import native
+from ..parallel.dp import build_buckets
+from ..parallel.topology import DPContext
+
+_ALIGN = 8  # elements per rank slice are a multiple of this (16-byte vectors)
+
+
+class _Bucket:
+    def __init__(self, params, dp: DPContext, device, dtype, late: bool, use_native: bool):
+        self.params = params
+        self.late = late
+        self.offsets, off = [], 0
+        for p in params:
+            self.offsets.append(off)
+            off += p.numel()
+        self.numel = off
+        n = dp.world
+        self.slice = -(-off // (n * _ALIGN)) * _ALIGN
+        self.padded = self.slice * n
+        esize = torch.tensor([], dtype=dtype).element_size()
+        if use_native:
+            from ..parallel.symm import PeerBuffer
+
+            self.gbuf = PeerBuffer(self.padded * esize, dp, device)
+            self.pbuf = PeerBuffer(self.padded * esize, dp, device)
+            self.grad = self.gbuf.view(dtype)
+            self.param = self.pbuf.view(dtype)
+        else:
+            self.gbuf = self.pbuf = None
+            self.grad = torch.zeros(self.padded, dtype=dtype, device=device)
+            self.param = torch.zeros(self.padded, dtype=dtype, device=device)
+        with torch.no_grad():
+            for p, o in zip(params, self.offsets):
+                self.param[o : o + p.numel()].copy_(p.data.reshape(-1))
+                p.data = self.param[o : o + p.numel()].view_as(p)
+        lo = dp.rank * self.slice
+        self.master = self.param[lo : lo + self.slice].float().clone()
+        self.exp_avg = torch.zeros_like(self.master)
+        self.exp_avg_sq = torch.zeros_like(self.master)
+        self.filled = set()
+        self.launched = False
+
+    def slot(self, i):
+        p = self.params[i]
+        return self.grad[self.offsets[i] : self.offsets[i] + p.numel()].view_as(p)
+
+    def stage(self, i) -> None:
+        g = self.params[i].grad
+        dst = self.slot(i)
+        if g is None:
+            dst.zero_()
+        elif g.data_ptr() != dst.data_ptr():
+            dst.copy_(g)
+
+
+class FusedDPAdam:
+    def __init__(
+        self,
+        model: torch.nn.Module,
+        dp: DPContext,
+        lr: float = 3e-4,
+        betas=(0.9, 0.999),
+        eps: float = 1e-8,
+        bucket_bytes: int = 25 * 1024 * 1024,
+        overlap: bool = True,
+    ):
+        self.dp = dp
+        self.lr, self.betas, self.eps = lr, tuple(betas), eps
+        self.model_params = [p for p in model.parameters() if p.requires_grad]
+        p0 = self.model_params[0]
+        self.device, self.dtype = p0.device, p0.dtype
+        self.native = p0.is_cuda and native.enabled()
+        if self.native and (self.dtype != torch.bfloat16 or dp.world > 8):
+            raise ValueError("fused DP Adam on CUDA needs bf16 parameters and at most 8 ranks")
+        order = self.model_params[::-1]
+        late = [p for p in order if getattr(p, "sequence_parallel_replicated", False)]
+        early = [p for p in order if not getattr(p, "sequence_parallel_replicated", False)]
+        groups = [(g, False) for g in build_buckets(early, bucket_bytes)] + ([(late, True)] if late else [])
+        self.buckets: List[_Bucket] = [
+            _Bucket(g, dp, self.device, self.dtype, is_late, self.native) for g, is_late in groups
+        ]
+        self._where = {}
+        for b in self.buckets:
+            for i, p in enumerate(b.params):
+                self._where[id(p)] = (b, i)
+        self._next = 0  # next bucket to launch (buckets launch in order)
+        self._step = 0
+        self._stepped = False
+        self.overlap = overlap
+        if self.native:
+            from ..parallel.symm import PeerBuffer
+
+            self.flags = PeerBuffer(64 * 4, dp, self.device)
+            self.done = torch.zeros(1, dtype=torch.int32, device=self.device)
+            self.epoch = 0
+            self.side = torch.cuda.Stream(device=self.device)
+        if overlap:
+            for p in order:
+                p.register_post_accumulate_grad_hook(self._hook)
+
+    # -- bookkeeping ------------------------------------------------------
+    def zero_grad(self, set_to_none: bool = True) -> None:
+        for p in self.model_params:
+            if set_to_none:
+                p.grad = None
+            elif p.grad is not None:
+                p.grad.zero_()
+
+    def _hook(self, p) -> None:
+        b, i = self._where[id(p)]
+        if b.late:
+            return  # staged in step(), after finalize_grads
+        b.stage(i)
+        b.filled.add(i)
+        self._launch_ready()
+
+    def _launch_ready(self) -> None:
+        while self._next < len(self.buckets):
+            b = self.buckets[self._next]
+            if b.late or len(b.filled) < len(b.params):
+                return
+            self._launch(b)
+            self._next += 1
+
+    def _launch(self, b: _Bucket) -> None:
+        if not self._stepped:
+            self._step += 1
+            self._stepped = True
+        b.launched = True
+        if self.native:
+            self._launch_native(b)
+        else:
+            self._launch_emulated(b)
+
+    def _launch_native(self, b: _Bucket) -> None:
+        self.epoch += 1
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.device))
+        self.side.wait_event(ev)
+        with torch.cuda.stream(self.side):
+            native.lib().fused_dp_adam(
+                b.gbuf.ptrs, b.pbuf.ptrs, self.flags.ptrs, b.master, b.exp_avg, b.exp_avg_sq, self.done,
+                b.slice, b.numel, self.dp.rank, self.epoch, self.lr, self.betas[0], self.betas[1], self.eps,
+                float(self._step),
+            )
+
+    def _launch_emulated(self, b: _Bucket) -> None:
+        g = b.grad.float()
+        if self.dp.enabled:
+            dist.all_reduce(g, group=self.dp.group)
+        lo = self.dp.rank * b.slice
+        gs = g[lo : lo + b.slice] / self.dp.world
+        beta1, beta2 = self.betas
+        bc1 = 1 - beta1**self._step
+        bc2 = 1 - beta2**self._step
+        valid = max(0, min(b.slice, b.numel - lo))
+        m, v, w = b.exp_avg[:valid], b.exp_avg_sq[:valid], b.master[:valid]
+        gv = gs[:valid]
+        m.lerp_(gv, 1 - beta1)
+        v.mul_(beta2).addcmul_(gv, gv, value=1 - beta2)
+        denom = (v.sqrt() / (bc2**0.5)).add_(self.eps)
+        w.addcdiv_(m, denom, value=-self.lr / bc1)
+        mine = b.master.to(self.dtype)
+        if self.dp.enabled:
+            parts = [torch.empty_like(mine) for _ in range(self.dp.world)]
+            dist.all_gather(parts, mine, group=self.dp.group)
+            full = torch.cat(parts)
+        else:
+            full = mine
+        with torch.no_grad():
+            b.param.copy_(full)
+
+    # -- optimizer API ------------------------------------------------------
+    def step(self) -> None:
+        for b in self.buckets:
+            if not b.launched:
+                for i in range(len(b.params)):
+                    if b.late or i not in b.filled:
+                        b.stage(i)
+                        b.filled.add(i)
+        self._launch_ready_all()
+        if self.native:
+            torch.cuda.current_stream(self.device).wait_stream(self.side)
+        for b in self.buckets:
+            b.filled = set()
+            b.launched = False
+        self._next = 0
+        self._stepped = False
+
+    def _launch_ready_all(self) -> None:
+        while self._next < len(self.buckets):
+            self._launch(self.buckets[self._next])
+            self._next += 1
+
+    # -- state access (checkpoints) ----------------------------------------
+    def full_state(self, p) -> Optional[dict]:
+        """Gather the full fp32 master / moments of parameter ``p`` (collective
+        over the DP group; call on every rank in the same order)."""
+        b, i = self._where[id(p)]
+        out = {}
+        for name, shard in (("master", b.master), ("exp_avg", b.exp_avg), ("exp_avg_sq", b.exp_avg_sq)):
+            if self.dp.enabled:
+                parts = [torch.empty_like(shard) for _ in range(self.dp.world)]
+                dist.all_gather(parts, shard.contiguous(), group=self.dp.group)
+                full = torch.cat(parts)
+            else:
+                full = shard
+            o = b.offsets[i]
+            out[name] = full[o : o + p.numel()].view_as(p).clone()
+        return out
+
+    def load_full_state(self, p, master, exp_avg, exp_avg_sq, step: int) -> None:
+        b, i = self._where[id(p)]
+        lo, hi = self.dp.rank * b.slice, (self.dp.rank + 1) * b.slice
+        o0, o1 = b.offsets[i], b.offsets[i] + p.numel()
+        a, z = max(lo, o0), min(hi, o1)
+        if a < z:
+            for shard, full in ((b.master, master), (b.exp_avg, exp_avg), (b.exp_avg_sq, exp_avg_sq)):
+                shard[a - lo : z - lo].copy_(full.reshape(-1)[a - o0 : z - o0].to(shard.device, shard.dtype))
+        self._step = int(step)

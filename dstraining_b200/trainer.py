@@ -17,12 +17,14 @@ step and reads the loss back to the host.
 from __future__ import annotations
 
 import argparse
+import os
 from typing import Optional
 
 import torch
 import torch.distributed as dist
 
 from .models.gpt import GPT, GPTChunks, GPTConfig, GPTStage
+from .optim.fused_dp import FusedDPAdam
 from .optim.precision import MasterWeightOptimizer
 from .parallel import topology
 from .parallel.dp import GradReducer, allreduce_gradients
@@ -99,12 +101,22 @@ class Trainer:
             self.pipe = Pipeline1F1B(model, self.pp, micro_batch_size=args.micro, seq_len=cfg.block_size)
         else:
             self.pipe = None
-        if args.bf16:
+        self.fused_dp = (
+            args.bf16 and self.dp.enabled and not args.naive_dp and self.device.type == "cuda"
+            and os.environ.get("DST_FUSED_DP", "1") != "0"
+        )
+        if self.fused_dp:
+            # DP reduction + fp32-master Adam + parameter all-gather in one
+            # NVLink kernel per bucket (sharded optimizer state).
+            self.opt = FusedDPAdam(
+                model, self.dp, lr=args.lr, bucket_bytes=int(args.bucket_mb * 1024 * 1024), overlap=self.pipe is None
+            )
+        elif args.bf16:
             self.opt = MasterWeightOptimizer(model.parameters(), lr=args.lr)
         else:
             self.opt = torch.optim.Adam(model.parameters(), lr=args.lr)
         self.reducer = None
-        if self.dp.enabled and not args.naive_dp:
+        if self.dp.enabled and not args.naive_dp and not self.fused_dp:
             self.reducer = GradReducer(
                 model, self.dp, bucket_bytes=int(args.bucket_mb * 1024 * 1024), overlap=self.pipe is None
             )
@@ -131,7 +143,7 @@ class Trainer:
             loss.backward()
         if self.reducer is not None:
             self.reducer.finish()
-        elif self.dp.enabled:
+        elif self.dp.enabled and not self.fused_dp:
             allreduce_gradients(self.model, self.dp)
         self.model.finalize_grads()
         self.opt.step()

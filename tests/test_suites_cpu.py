@@ -86,3 +86,8 @@ def test_train_cli_all_axes_and_resume(tmp_path):
     assert launch(8, [train, "--steps", "6", "--resume", *common], timeout=540, env=env) == 0
     lines = open(tmp_path / "m.jsonl").read().splitlines()
     assert len(lines) == 6  # steps 0-3, then 4-5 after the resume
+
+
+@pytest.mark.parametrize("n,args", [(2, ("--dp", "2")), (4, ("--dp", "2", "--tp", "2", "--sp")), (4, ("--dp", "4",))])
+def test_fused_dp_suite(n, args):
+    run(n, "fused_dp_suite.py", *args)
