@@ -45,4 +45,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_attn(m);
   register_attn_tc(m);
   register_symm(m);
+  register_tp(m);
 }

@@ -28,3 +28,4 @@ void register_ce(pybind11::module& m);
 void register_attn(pybind11::module& m);
 void register_attn_tc(pybind11::module& m);
 void register_symm(pybind11::module& m);
+void register_tp(pybind11::module& m);

@@ -58,10 +58,10 @@ int num_sms() {
   return n[dev];
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
+template <int BN, bool A_MN, bool B_MN, int EPI, int GATHER = 0, bool SCATTER = false>
 static void launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const CUtensorMap& tx,
-                       const GemmParams& p, int grid, cudaStream_t st) {
-  auto kern = gemm_bf16_kernel<BN, A_MN, B_MN, EPI>;
+                       const GemmParams& p, int grid, cudaStream_t st, const PeerArgs* pa = nullptr) {
+  auto kern = gemm_bf16_kernel<BN, A_MN, B_MN, EPI, GATHER, SCATTER>;
   constexpr int smem = GemmCfg<BN>::kSmemBytes;
   static bool configured[64] = {false};
   int dev;
@@ -70,7 +70,8 @@ static void launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     configured[dev] = true;
   }
-  kern<<<grid, kGemmThreads, smem, st>>>(ta, tb, to, tx, p);
+  static const PeerArgs none{};
+  kern<<<grid, kGemmThreads, smem, st>>>(ta, tb, to, tx, p, pa ? *pa : none);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -305,6 +306,20 @@ at::Tensor colsum_bf16(const at::Tensor& x) {
   return out;
 }
 
+// Sum a split-K fp32 workspace [splits, M, N] in split order -> bf16 [M, N].
+at::Tensor splitk_reduce(const at::Tensor& ws) {
+  TORCH_CHECK(ws.is_cuda() && ws.scalar_type() == at::kFloat && ws.dim() == 3 && ws.is_contiguous(), "splitk_reduce: ws");
+  c10::cuda::CUDAGuard g(ws.device());
+  const int s = ws.size(0), M = ws.size(1), N = ws.size(2);
+  TORCH_CHECK(N % 4 == 0, "splitk_reduce: N must be a multiple of 4");
+  at::Tensor out = at::empty({M, N}, ws.options().dtype(at::kBFloat16));
+  const size_t mn = static_cast<size_t>(M) * N;
+  splitk_reduce_kernel<<<static_cast<int>((mn / 4 + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      ws.data_ptr<float>(), s, mn, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), nullptr);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return out;
+}
+
 // Fused LM-head forward: logits (bf16, optional) and per-(row, tile) softmax
 // statistics from the fp32 accumulator, target logits for targets inside
 // this shard. Returns (logits, tile_max, tile_sum, tgt_logit).
@@ -336,6 +351,180 @@ std::vector<at::Tensor> gemm_ce_stats(const at::Tensor& X, const at::Tensor& W, 
   return {logits, tmax, tsum, tgt};
 }
 
+// ---------------------------------------------------------------- tensor parallel
+// Peer-aware GEMM (gemm.cuh): mode 1 gathers operand A over the TP group,
+// mode 2 gathers operand B, mode 3 scatters the output into the owning
+// ranks' receive slots. `peers` holds each rank's base pointer of the
+// gathered shard (modes 1, 2) or of the receive buffer (mode 3); `flags`
+// each rank's flag words of this channel; `epoch` the channel's launch count.
+template <int BN, bool A_MN, bool B_MN, int MODE>
+static void peer_dispatch(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+                          const CUtensorMap& tx, const GemmParams& p, int grid, cudaStream_t st, const PeerArgs& pa) {
+  constexpr int G = MODE == 3 ? 0 : MODE;
+  constexpr bool SC = MODE == 3;
+  if constexpr (MODE == 1 && !A_MN && !B_MN) {
+    switch (epi) {
+      case kEpiStore: return launch_one<BN, A_MN, B_MN, kEpiStore, G, SC>(ta, tb, to, ta, p, grid, st, &pa);
+      case kEpiBias: return launch_one<BN, A_MN, B_MN, kEpiBias, G, SC>(ta, tb, to, ta, p, grid, st, &pa);
+      case kEpiBiasGelu: return launch_one<BN, A_MN, B_MN, kEpiBiasGelu, G, SC>(ta, tb, to, tx, p, grid, st, &pa);
+      case kEpiCEStats: return launch_one<BN, A_MN, B_MN, kEpiCEStats, G, SC>(ta, tb, to, ta, p, grid, st, &pa);
+      default: break;
+    }
+  } else if constexpr (MODE == 1 && !A_MN && B_MN) {
+    switch (epi) {
+      case kEpiStore: return launch_one<BN, A_MN, B_MN, kEpiStore, G, SC>(ta, tb, to, ta, p, grid, st, &pa);
+      case kEpiDGelu: return launch_one<BN, A_MN, B_MN, kEpiDGelu, G, SC>(ta, tb, to, ta, p, grid, st, &pa);
+      default: break;
+    }
+  } else if constexpr ((MODE == 1 || MODE == 2) && A_MN && B_MN) {
+    switch (epi) {
+      case kEpiPartialF32: return launch_one<BN, A_MN, B_MN, kEpiPartialF32, G, SC>(ta, tb, to, ta, p, grid, st, &pa);
+      case kEpiStore: return launch_one<BN, A_MN, B_MN, kEpiStore, G, SC>(ta, tb, to, ta, p, grid, st, &pa);
+      default: break;
+    }
+  } else if constexpr (MODE == 3 && !A_MN) {
+    if (epi == kEpiStore) return launch_one<BN, A_MN, B_MN, kEpiStore, G, SC>(ta, tb, to, ta, p, grid, st, &pa);
+  }
+  TORCH_CHECK(false, "tp_gemm: unsupported mode/layout/epilogue combination");
+}
+
+template <int BN, int MODE>
+static void peer_layout(bool a_mn, bool b_mn, int epi, const CUtensorMap& ta, const CUtensorMap& tb,
+                        const CUtensorMap& to, const CUtensorMap& tx, const GemmParams& p, int grid, cudaStream_t st,
+                        const PeerArgs& pa) {
+  if (!a_mn && !b_mn) return peer_dispatch<BN, false, false, MODE>(epi, ta, tb, to, tx, p, grid, st, pa);
+  if (!a_mn && b_mn) return peer_dispatch<BN, false, true, MODE>(epi, ta, tb, to, tx, p, grid, st, pa);
+  if (a_mn && b_mn) return peer_dispatch<BN, true, true, MODE>(epi, ta, tb, to, tx, p, grid, st, pa);
+  TORCH_CHECK(false, "tp_gemm: unsupported layout");
+}
+
+// Returns the bf16 output (modes 1, 2 with a bf16 epilogue), the fp32 split-K
+// workspace (PartialF32), or an empty tensor (mode 3: the data went to the
+// peers). The gathered dimension of size `tokens` is split evenly over the
+// group; `seq` is the per-batch sequence length of that dimension.
+std::vector<at::Tensor> tp_gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, int64_t M, int64_t N,
+                                int64_t K, int64_t epi, int64_t mode, const std::vector<int64_t>& peers,
+                                const std::vector<int64_t>& flags, const at::Tensor& done, int64_t rank, int64_t seq,
+                                int64_t epoch, int64_t splits, const c10::optional<at::Tensor>& bias,
+                                const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& aux_out,
+                                const c10::optional<at::Tensor>& targets, int64_t ce_col0, int64_t ce_valid) {
+  check_bf16_2d(A, "A");
+  check_bf16_2d(B, "B");
+  c10::cuda::CUDAGuard g(A.device());
+  const int tp = static_cast<int>(peers.size());
+  TORCH_CHECK(tp >= 2 && tp <= kMaxPeers && flags.size() == peers.size(), "tp_gemm: 2..8 ranks");
+  TORCH_CHECK(mode >= 1 && mode <= 3, "tp_gemm: mode");
+  const int64_t tokens = (mode == 3 || (mode == 1 && !a_mn)) ? M : K;
+  TORCH_CHECK(tokens % seq == 0 && seq % tp == 0, "tp_gemm: token dimension must split evenly");
+  const int seq_local = static_cast<int>(seq / tp);
+  const int rows_local = static_cast<int>(tokens / tp);
+  const int BN = (N >= 256) ? 256 : 128;
+  if (mode == 1 && !a_mn) TORCH_CHECK(seq_local % kBM == 0, "tp_gemm: T/tp must be a multiple of 128");
+  if (mode == 3) TORCH_CHECK(seq_local % 32 == 0, "tp_gemm: T/tp must be a multiple of 32");
+  if ((mode == 1 && a_mn) || mode == 2) TORCH_CHECK(seq_local % kBK == 0, "tp_gemm: T/tp must be a multiple of 64");
+
+  PeerArgs pa{};
+  pa.tp = tp;
+  pa.rank = static_cast<int>(rank);
+  pa.seq = static_cast<int>(seq);
+  pa.seq_local = seq_local;
+  pa.rows_local = rows_local;
+  pa.epoch = static_cast<uint32_t>(epoch);
+  pa.done_ctas = reinterpret_cast<unsigned int*>(done.data_ptr<int32_t>());
+  for (int r = 0; r < tp; ++r) pa.flags[r] = reinterpret_cast<uint32_t*>(flags[r]);
+
+  // Local operand maps (the gathered one is only a shape template).
+  CUtensorMap ta = a_mn ? make_tmap_bf16(A.data_ptr(), A.size(1), A.size(0), A.stride(0), 64, 64)
+                        : make_tmap_bf16(A.data_ptr(), A.size(1), A.size(0), A.stride(0), 64, kBM);
+  CUtensorMap tb = b_mn ? make_tmap_bf16(B.data_ptr(), B.size(1), B.size(0), B.stride(0), 64, 64)
+                        : make_tmap_bf16(B.data_ptr(), B.size(1), B.size(0), B.stride(0), 64, BN);
+  const at::Tensor& G = (mode == 2) ? B : A;
+  const bool g_mn = (mode == 2) ? b_mn : a_mn;
+  if (mode == 1 || mode == 2) {
+    for (int r = 0; r < tp; ++r)
+      pa.gather[r] = make_tmap_bf16(reinterpret_cast<void*>(peers[r]), G.size(1), G.size(0), G.stride(0), 64,
+                                    g_mn ? 64 : kBM);
+  } else {
+    for (int r = 0; r < tp; ++r)
+      pa.scatter[r] = make_tmap_bf16(reinterpret_cast<void*>(peers[r]), N, static_cast<uint64_t>(tp) * rows_local, N,
+                                     kEpiChunk, 32);
+  }
+
+  GemmParams p{};
+  std::vector<at::Tensor> result;
+  at::Tensor out, ws;
+  int s = 1;
+  const int k_blocks = static_cast<int>((K + kBK - 1) / kBK);
+  if (epi == kEpiPartialF32) {
+    s = splits > 0 ? static_cast<int>(splits) : gemm_splits_for(M, N, K);
+    s = std::max(1, std::min(s, k_blocks));
+    const int per = (k_blocks + s - 1) / s;
+    s = (k_blocks + per - 1) / per;
+    ws = at::empty({s, M, N}, A.options().dtype(at::kFloat));
+    p.ws = ws.data_ptr<float>();
+    result.push_back(ws);
+  } else if (mode != 3) {
+    out = at::empty({M, N}, A.options());
+    p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+    p.ldo = N;
+    result.push_back(out);
+  } else {
+    result.push_back(at::Tensor());
+  }
+  if (bias.has_value()) p.bias = reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr());
+  if (aux.has_value()) {
+    check_bf16_2d(*aux, "aux");
+    p.aux = reinterpret_cast<const __nv_bfloat16*>(aux->data_ptr());
+    p.ld_aux = aux->stride(0);
+  }
+  at::Tensor pre;
+  if (epi == kEpiBiasGelu) {
+    TORCH_CHECK(mode == 1, "tp_gemm: the GELU epilogue is offered in gather mode only");
+    pre = at::empty({M, N}, A.options());  // pre-activation, returned after the output
+  }
+  at::Tensor tmax, tsum, tgt;
+  if (epi == kEpiCEStats) {
+    TORCH_CHECK(targets.has_value(), "tp_gemm: CE statistics need targets");
+    const int n_tiles = static_cast<int>((N + BN - 1) / BN);
+    tmax = at::empty({M, n_tiles}, A.options().dtype(at::kFloat));
+    tsum = at::empty({M, n_tiles}, A.options().dtype(at::kFloat));
+    tgt = at::zeros({M}, A.options().dtype(at::kFloat));
+    p.ce_max = tmax.data_ptr<float>();
+    p.ce_sum = tsum.data_ptr<float>();
+    p.ce_tgt = tgt.data_ptr<float>();
+    p.ce_targets = targets->data_ptr<int64_t>();
+    p.ce_col0 = static_cast<int>(ce_col0);
+    p.ce_valid_cols = static_cast<int>(ce_valid);
+    result.push_back(tmax);
+    result.push_back(tsum);
+    result.push_back(tgt);
+  }
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.splits = s;
+  p.k_blocks_per_split = (k_blocks + s - 1) / s;
+  p.status = status_ptr();
+  CUtensorMap to = ta, tx = ta;
+  if (mode != 3 && epi != kEpiPartialF32) to = make_tmap_bf16(p.out, N, M, N, kEpiChunk, 32);
+  if (epi == kEpiBiasGelu) {
+    p.aux_out = reinterpret_cast<__nv_bfloat16*>(pre.data_ptr());
+    tx = make_tmap_bf16(pre.data_ptr(), N, M, N, kEpiChunk, 32);
+    result.push_back(pre);
+  }
+  const int tiles = static_cast<int>(((M + kBM - 1) / kBM) * ((N + BN - 1) / BN));
+  const int grid = std::min(tiles * s, num_sms());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+#define PEER_MODE(BNV, MV) peer_layout<BNV, MV>(a_mn, b_mn, static_cast<int>(epi), ta, tb, to, tx, p, grid, st, pa)
+  if (BN == 256) {
+    if (mode == 1) PEER_MODE(256, 1); else if (mode == 2) PEER_MODE(256, 2); else PEER_MODE(256, 3);
+  } else {
+    if (mode == 1) PEER_MODE(128, 1); else if (mode == 2) PEER_MODE(128, 2); else PEER_MODE(128, 3);
+  }
+#undef PEER_MODE
+  return result;
+}
+
 void register_gemm(pybind11::module& m) {
   m.def("gemm", &gemm, "bf16 tcgen05 GEMM with fused epilogue", py::arg("A"), py::arg("a_mn"), py::arg("B"),
         py::arg("b_mn"), py::arg("epi"), py::arg("bias") = py::none(), py::arg("aux") = py::none(),
@@ -343,5 +532,12 @@ void register_gemm(pybind11::module& m) {
   m.def("gemm_splitk", &gemm_splitk, "split-K bf16 GEMM with deterministic fp32 reduction", py::arg("A"),
         py::arg("a_mn"), py::arg("B"), py::arg("b_mn"), py::arg("splits") = 0, py::arg("accum_f32") = py::none());
   m.def("colsum_bf16", &colsum_bf16, "column sums of a bf16 matrix (bias gradient)");
+  m.def("splitk_reduce", &splitk_reduce, "sum a split-K fp32 workspace in split order to bf16");
   m.def("gemm_ce_stats", &gemm_ce_stats, "LM-head GEMM with fused softmax statistics");
+  m.def("tp_gemm", &tp_gemm, "tensor-parallel GEMM fused with an NVLink all-gather (modes 1, 2) or reduce-scatter (mode 3)",
+        py::arg("A"), py::arg("a_mn"), py::arg("B"), py::arg("b_mn"), py::arg("M"), py::arg("N"), py::arg("K"),
+        py::arg("epi"), py::arg("mode"), py::arg("peers"), py::arg("flags"), py::arg("done"), py::arg("rank"),
+        py::arg("seq"), py::arg("epoch"), py::arg("splits") = 0, py::arg("bias") = py::none(),
+        py::arg("aux") = py::none(), py::arg("aux_out") = py::none(), py::arg("targets") = py::none(),
+        py::arg("ce_col0") = 0, py::arg("ce_valid") = 0);
 }

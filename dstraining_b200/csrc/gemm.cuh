@@ -67,6 +67,60 @@ struct GemmParams {
   int* status;
 };
 
+// ---------------------------------------------------------------- TP peers
+// Tensor parallelism with sequence sharding: the token dimension (rows of
+// [B*T, C] activations) is split so that rank r holds, for every batch row b,
+// tokens [r*Tl, (r+1)*Tl) with Tl = T / tp, stored as local rows b*Tl + t.
+//
+// Gather mode (AG + GEMM): the operand whose token dimension is sharded is
+// TMA-loaded tile by tile directly from the owning rank's buffer (a plain,
+// single-CTA TMA load from peer memory over NVLink). For a K-major operand
+// the tokens are its rows; for an MN-major operand they are the K dimension.
+// Scatter mode (GEMM + reduce-scatter): each 32-row chunk of the output is
+// TMA-stored straight into the owning rank's receive slot [src rank][local
+// row][N] over NVLink while later tiles are still being computed; a separate
+// reduction sums the slots (tp_reduce in tp.cu).
+//
+// Flags (per channel, kinds x 8 ranks, epochs identical on every rank):
+enum PeerFlag : int {
+  kGReady = 0,     // my gathered-operand shard is complete
+  kGConsumed = 1,  // I have finished reading every peer's shard
+  kSWritten = 2,   // all my scatter stores into your receive slots are complete
+  kSConsumed = 3,  // I have finished reading my receive slots
+  kAGWritten = 4,  // (all-reduce form) my reduced rows are in every rank's output
+};
+constexpr int kMaxPeers = 8;
+
+struct PeerArgs {
+  CUtensorMap gather[kMaxPeers];   // each rank's gathered operand (same shape as the local one)
+  CUtensorMap scatter[kMaxPeers];  // each rank's receive buffer [tp * rows_local, N]
+  uint32_t* flags[kMaxPeers];      // each rank's flag words for this channel [kinds][8]
+  unsigned int* done_ctas;         // this rank's CTA completion counter (self-resetting)
+  int tp, rank;
+  int seq;         // T (tokens per batch row of the gathered / scattered tensor)
+  int seq_local;   // T / tp
+  int rows_local;  // B * T / tp (rows of one receive slot)
+  uint32_t epoch;
+};
+
+// Global token index -> (owning rank, row in the owner's local shard).
+__device__ __forceinline__ void token_owner(const PeerArgs& pa, int tok, int& src, int& local) {
+  const int b = tok / pa.seq, t = tok - b * pa.seq;
+  src = t / pa.seq_local;
+  local = b * pa.seq_local + (t - src * pa.seq_local);
+}
+
+__device__ __forceinline__ void peer_publish(const PeerArgs& pa, int kind, uint32_t epoch) {
+  __threadfence_system();
+  for (int p = 0; p < pa.tp; ++p) flag_store_release(pa.flags[p] + kind * kMaxPeers + pa.rank, epoch);
+}
+
+__device__ __forceinline__ bool peer_wait_all(const PeerArgs& pa, int kind, uint32_t epoch, int* status) {
+  for (int p = 0; p < pa.tp; ++p)
+    if (!flag_wait_geq(pa.flags[pa.rank] + kind * kMaxPeers + p, epoch, status, kTimeoutPeer)) return false;
+  return true;
+}
+
 constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kGemmThreads = 192;
@@ -122,13 +176,18 @@ __device__ __forceinline__ void stage_bf16x32(uint8_t* tile, int lane, int half,
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
+// GATHER: 0 none, 1 operand A gathered over TP, 2 operand B gathered.
+// SCATTER: bf16 output chunks go to the owning rank's receive slot.
+template <int BN, bool A_MN, bool B_MN, int EPI, int GATHER = 0, bool SCATTER = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmAux,
-                     GemmParams p) {
+                     GemmParams p, const __grid_constant__ PeerArgs pa) {
   using Cfg = GemmCfg<BN>;
   constexpr int S = Cfg::kStages;
+  static_assert(!(SCATTER && (EPI == kEpiPartialF32 || EPI == kEpiAccumF32 || EPI == kEpiBiasGelu ||
+                              EPI == kEpiCEStats)),
+                "scatter mode takes a plain bf16 output");
   constexpr bool kF32Out = (EPI == kEpiPartialF32 || EPI == kEpiAccumF32);
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the 128B swizzle atoms.
@@ -175,6 +234,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Gather mode: this rank's shard was completed by earlier kernels on the
+  // stream; announce it before anyone waits for a peer's.
+  if (GATHER != 0 && blockIdx.x == 0 && threadIdx.x == 0) peer_publish(pa, kGReady, pa.epoch);
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -182,6 +244,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      uint32_t ready_mask = 0;  // gather sources whose shard is known ready
+      auto source = [&](int tok, int& local) -> const CUtensorMap* {
+        int src;
+        token_owner(pa, tok, src, local);
+        if (!(ready_mask & (1u << src))) {
+          if (!flag_wait_geq(pa.flags[pa.rank] + kGReady * kMaxPeers + src, pa.epoch, p.status, kTimeoutPeer))
+            return nullptr;
+          ready_mask |= 1u << src;
+        }
+        return &pa.gather[src];
+      };
       for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
         const int tile = u % num_tiles;
         const int split = u / num_tiles;
@@ -196,19 +269,37 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           uint8_t* sa = stage_base + stage * Cfg::kStageBytes;
           uint8_t* sb = sa + Cfg::kStageA;
-          mbar_arrive_expect_tx(&full_bar[stage], Cfg::kStageBytes);
           const int k0 = kb * kBK;
+          // Operand sources: local tensor maps, or (gather mode) the owning
+          // rank's shard for the token coordinate of the gathered operand.
+          const CUtensorMap* mapA = &tmA;
+          const CUtensorMap* mapB = &tmB;
+          int a_m = m0, a_k = k0, b_n = n0, b_k = k0;
+          if (GATHER == 1) {
+            mapA = A_MN ? source(k0, a_k) : source(m0, a_m);
+            if (mapA == nullptr) {
+              ok = false;
+              break;
+            }
+          } else if (GATHER == 2) {
+            mapB = B_MN ? source(k0, b_k) : source(n0, b_n);
+            if (mapB == nullptr) {
+              ok = false;
+              break;
+            }
+          }
+          mbar_arrive_expect_tx(&full_bar[stage], Cfg::kStageBytes);
           if (!A_MN) {
-            tma_load_2d(sa, &tmA, &full_bar[stage], k0, m0);
+            tma_load_2d(sa, mapA, &full_bar[stage], a_k, a_m);
           } else {
 #pragma unroll
-            for (int j = 0; j < kBM / 64; ++j) tma_load_2d(sa + j * 64 * kBK * 2, &tmA, &full_bar[stage], m0 + 64 * j, k0);
+            for (int j = 0; j < kBM / 64; ++j) tma_load_2d(sa + j * 64 * kBK * 2, mapA, &full_bar[stage], a_m + 64 * j, a_k);
           }
           if (!B_MN) {
-            tma_load_2d(sb, &tmB, &full_bar[stage], k0, n0);
+            tma_load_2d(sb, mapB, &full_bar[stage], b_k, b_n);
           } else {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + j * 64 * kBK * 2, &tmB, &full_bar[stage], n0 + 64 * j, k0);
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + j * 64 * kBK * 2, mapB, &full_bar[stage], b_n + 64 * j, b_k);
           }
           if (++stage == S) {
             stage = 0;
@@ -273,6 +364,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     float* my_bias = bias_stage + (warp - 2) * kEpiChunk;
     int iter = 0;
     int chunk_count = 0;
+    uint32_t scatter_ok = 0;  // owners whose receive slot is known drained (lane 0)
     for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++iter) {
       const int tile = u % num_tiles;
       const int split = u / num_tiles;
@@ -392,8 +484,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tmOut, tile_a, col0, m0 + quad * 32);
-            if (EPI == kEpiBiasGelu) tma_store_2d(&tmAux, tile_b, col0, m0 + quad * 32);
+            if (SCATTER) {
+              // This 32-row chunk belongs to one rank's sequence shard: store it
+              // into that rank's receive slot for this source rank, once the
+              // owner has drained the slot's previous contents.
+              int owner, local;
+              token_owner(pa, m0 + quad * 32, owner, local);
+              if (!(scatter_ok & (1u << owner))) {
+                if (flag_wait_geq(pa.flags[pa.rank] + kSConsumed * kMaxPeers + owner, pa.epoch - 1, p.status,
+                                  kTimeoutPeer))
+                  scatter_ok |= 1u << owner;
+              }
+              if (scatter_ok & (1u << owner))
+                tma_store_2d(&pa.scatter[owner], tile_a, col0, pa.rank * pa.rows_local + local);
+            } else {
+              tma_store_2d(&tmOut, tile_a, col0, m0 + quad * 32);
+              if (EPI == kEpiBiasGelu) tma_store_2d(&tmAux, tile_b, col0, m0 + quad * 32);
+            }
             bulk_commit();
           }
         }
@@ -416,6 +523,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+  if ((GATHER != 0 || SCATTER) && threadIdx.x == 0) {
+    // Every CTA's loads have been consumed by its MMAs and its stores have
+    // completed; the last CTA to get here speaks for the whole launch.
+    __threadfence_system();
+    const unsigned int prev = atomicAdd(pa.done_ctas, 1u);
+    if (prev == gridDim.x - 1) {
+      atomicExch(pa.done_ctas, 0u);
+      if (SCATTER) peer_publish(pa, kSWritten, pa.epoch);
+      if (GATHER != 0) {
+        // Peers may overwrite their shards only after everyone has read them.
+        peer_publish(pa, kGConsumed, pa.epoch);
+        peer_wait_all(pa, kGConsumed, pa.epoch, p.status);
+      }
+    }
   }
 }
 

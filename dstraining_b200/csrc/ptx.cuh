@@ -51,6 +51,33 @@ __device__ __forceinline__ void record_status(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
 }
 
+// ---------------------------------------------------------------- cross-GPU flags
+// 32-bit progress flags in peer memory: a rank stores a launch epoch into a
+// peer's flag word with release semantics at system scope; a waiter loads its
+// own flag words with acquire semantics (wrap-safe comparison).
+__device__ __forceinline__ void flag_store_release(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t flag_load_acquire(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait until *flag >= epoch.
+__device__ __forceinline__ bool flag_wait_geq(const uint32_t* flag, uint32_t epoch, int* status, int code) {
+  if (static_cast<int32_t>(flag_load_acquire(flag) - epoch) >= 0) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (static_cast<int32_t>(flag_load_acquire(flag) - epoch) < 0) {
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      record_status(status, code);
+      return false;
+    }
+  }
+  return true;
+}
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));

@@ -7,6 +7,11 @@ over the logits. Per-tile stats merge in tile order into per-row stats; under
 TP the ``[3, N]`` per-rank stats are all-gathered and merged in rank order
 (one collective; bitwise identical on every rank).
 
+With sequence parallelism the head's input arrives sequence-sharded: the GEMM
+gathers it from the peers itself (gather mode of ``tp_gemm``), the dX of the
+backward leaves through the scatter-mode GEMM + slot reduction (the
+reduce-scatter), and dW gathers the input again along its K dimension.
+
 Backward turns the saved bf16 logits into ``(softmax - onehot) * grad / N`` in
 place and runs the two backward GEMMs (dX = dlogits W, dW = dlogits^T X) on
 them. Same math as :mod:`dstraining_b200.ops.cross_entropy`.
@@ -19,6 +24,7 @@ import torch
 from ..ops import native
 from ..parallel.comm import all_gather_dim, all_reduce_sum, reduce_scatter_dim
 from ..parallel.topology import TPContext
+from . import tp_fused
 from .cross_entropy import merge_stats
 from .gemm import EPI_STORE, gemm
 
@@ -27,14 +33,23 @@ class _FusedHeadCE(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w, targets, tp, real_vocab, seq_parallel):
         lib = native.lib()
-        if seq_parallel and tp.enabled:
-            x = all_gather_dim(x, tp, 1)
-        x2 = x.reshape(-1, x.shape[-1]).contiguous()
         tg = targets.reshape(-1).contiguous()
         v_local = w.shape[0]
         col0 = tp.rank * v_local
         valid = max(0, min(v_local, real_vocab - col0))
-        logits, tmax, tsum, tgt = lib.gemm_ce_stats(x2, w, tg, col0, valid)
+        seq = x.shape[1] * tp.world if (seq_parallel and tp.enabled) else x.shape[1]
+        fused_sp = seq_parallel and tp.enabled and tp_fused.usable(tp, seq)
+        if fused_sp:
+            x2 = x.reshape(-1, x.shape[-1]).contiguous()  # this rank's sequence shard
+            logits, tmax, tsum, tgt = tp_fused.ag_gemm(
+                id(w), "head.fwd", tp, x2, seq, w, False, tp_fused.EPI_CE_STATS, targets=tg, ce_col0=col0,
+                ce_valid=valid,
+            )
+        else:
+            if seq_parallel and tp.enabled:
+                x = all_gather_dim(x, tp, 1)
+            x2 = x.reshape(-1, x.shape[-1]).contiguous()
+            logits, tmax, tsum, tgt = lib.gemm_ce_stats(x2, w, tg, col0, valid)
         m, s = lib.ce_merge_tiles(tmax, tsum)
         stats = torch.stack([m, s, tgt])[None]
         if tp.enabled:
@@ -42,16 +57,20 @@ class _FusedHeadCE(torch.autograd.Function):
         lse, tgt_all = merge_stats(stats)
         loss = (lse - tgt_all).mean()
         ctx.save_for_backward(logits, lse, x2, w, tg)
-        ctx.meta = (tp, seq_parallel, col0, valid, x.shape)
+        ctx.meta = (tp, seq_parallel, col0, valid, x.shape, fused_sp, seq, id(w))
         return loss
 
     @staticmethod
     def backward(ctx, g):
         logits, lse, x2, w, tg = ctx.saved_tensors
-        tp, seq_parallel, col0, valid, xshape = ctx.meta
+        tp, seq_parallel, col0, valid, xshape, fused_sp, seq, k = ctx.meta
         lib = native.lib()
         n = logits.shape[0]
         lib.ce_grad_inplace(logits, lse.contiguous(), tg, col0, valid, g.float().reshape(1).contiguous(), 1.0 / n)
+        if fused_sp:
+            dx = tp_fused.gemm_rs(k, "head.bwd.rs", tp, logits, seq, w, True).view(xshape)
+            dw = tp_fused.dw_gather_b(k, "head.bwd.x", tp, logits, x2, seq, split=False)
+            return dx, dw, None, None, None, None
         dx = gemm(logits, False, w, True, EPI_STORE).view(xshape)
         dw = gemm(logits, True, x2, True, EPI_STORE)
         if tp.enabled:

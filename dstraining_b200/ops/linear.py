@@ -22,6 +22,7 @@ import torch
 
 from ..parallel.comm import all_gather_dim, all_reduce_sum, reduce_scatter_dim
 from ..parallel.topology import TPContext
+from . import tp_fused
 from .gemm import EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_RESID, EPI_DGELU, EPI_STORE, bias_grad, gemm, weight_grad
 
 SEQ = 1
@@ -175,15 +176,31 @@ class _MLPFn(torch.autograd.Function):
         return _enter_bwd(dx, tp, in_mode), dw1, db1, dw2, db2, dres, None, None, None
 
 
+def _seq_len(x: torch.Tensor, tp: TPContext, sharded: bool) -> int:
+    return x.shape[1] * tp.world if sharded else x.shape[1]
+
+
 def column_parallel_linear(x, w, b, tp: TPContext, mode: str, activation: Optional[str]):
+    if activation is None and x.dim() == 3 and tp_fused.usable(tp, _seq_len(x, tp, mode == "sequence")):
+        return tp_fused.column_parallel(x, w, b, tp, mode)
     return _ColumnFn.apply(x, w, b, tp, mode, activation == "gelu_tanh")
 
 
 def row_parallel_linear(x, w, b, tp: TPContext, mode: str, residual: Optional[torch.Tensor]):
+    if x.dim() == 3 and tp_fused.usable(tp, x.shape[1]):
+        return tp_fused.row_parallel(x, w, b, residual, tp, mode)
     return _RowFn.apply(x, w, b, residual, tp, mode)
 
 
 def mlp(x, c_fc, c_proj, residual: Optional[torch.Tensor]):
+    tp = c_fc.tp
+    if (
+        c_fc.input_mode == "sequence"
+        and c_proj.output_mode == "sequence"
+        and x.dim() == 3
+        and tp_fused.usable(tp, x.shape[1] * tp.world)
+    ):
+        return tp_fused.mlp_sequence_parallel(x, c_fc.weight, c_fc.bias, c_proj.weight, c_proj.bias, residual, tp)
     return _MLPFn.apply(
         x, c_fc.weight, c_fc.bias, c_proj.weight, c_proj.bias, residual, c_fc.tp, c_fc.input_mode, c_proj.output_mode
     )

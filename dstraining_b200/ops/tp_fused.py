@@ -1,0 +1,270 @@
+"""Tensor-parallel layers with the collective fused into the GEMM (CUDA bf16).
+
+Every TP collective of the Megatron layer pair runs inside a tcgen05 GEMM
+kernel over NVLink peer memory (``tp_gemm`` in ``csrc/gemm.cu``):
+
+* gather (AG + GEMM): the sequence-sharded operand is TMA-loaded tile by tile
+  straight from the owning rank's buffer - the column-parallel forward
+  (``g``), the row-parallel dX (``ḡ`` backward), and the gathered operand of
+  the weight-gradient GEMMs;
+* scatter (GEMM + reduce-scatter): each 32-row output chunk is TMA-stored into
+  the owning rank's receive slot as soon as it is computed; ``tp_reduce`` then
+  sums the slots in rank order with the bias and residual - the row-parallel
+  forward (``ḡ``) and the column-parallel dX (``g`` backward).
+
+Without sequence parallelism (replicated activations) the all-reduces ``f̄``
+and ``f``'s backward are the scatter GEMM + reduce followed by a peer
+all-gather of the reduced shards (``tp_allgather``).
+
+Each call site owns a :class:`_Channel`: a peer buffer for the shard (or the
+receive slots), the cross-rank flag words and a launch epoch. Channels are
+created lazily, in the same order on every rank of the group (the model runs
+the same code on each), and grown when a larger activation arrives. The
+kernels' flag protocol makes reusing a channel safe: a shard buffer is not
+rewritten before every peer has read it, a receive slot is not rewritten
+before its owner has drained it.
+"""
+
+from __future__ import annotations
+
+from typing import Dict, Optional, Tuple
+
+import torch
+
+from ..parallel.symm import PeerBuffer
+from ..parallel.topology import TPContext
+from . import native
+from .gemm import EPI_BIAS, EPI_BIAS_GELU, EPI_DGELU, EPI_STORE, bias_grad, gemm, weight_grad
+
+EPI_PARTIAL_F32 = 5
+EPI_CE_STATS = 6
+MODE_GATHER_A, MODE_GATHER_B, MODE_SCATTER = 1, 2, 3
+
+
+class _Channel:
+    def __init__(self, tp: TPContext, device: torch.device, nbytes: int):
+        self.tp = tp
+        self.buf = PeerBuffer(nbytes, tp, device)
+        self.flags = PeerBuffer(64 * 4, tp, device)
+        self.done = torch.zeros(1, dtype=torch.int32, device=device)
+        self.epoch = 0
+        self.nbytes = nbytes
+
+    def next_epoch(self) -> int:
+        self.epoch += 1
+        return self.epoch
+
+    def view(self, numel: int) -> torch.Tensor:
+        return self.buf.view(torch.bfloat16)[:numel]
+
+
+_CHANNELS: Dict[Tuple[int, str], _Channel] = {}
+
+
+def channel(owner: int, role: str, tp: TPContext, nbytes: int, device: torch.device) -> _Channel:
+    """The channel of one call site, keyed by the owning layer (the id of its
+    weight Parameter, captured in forward) and a role; created or grown
+    collectively in program order."""
+    key = (owner, role)
+    ch = _CHANNELS.get(key)
+    if ch is None or ch.nbytes < nbytes:
+        ch = _Channel(tp, device, nbytes)
+        _CHANNELS[key] = ch
+    return ch
+
+
+def _flat(t: torch.Tensor) -> torch.Tensor:
+    return t.reshape(-1, t.shape[-1])
+
+
+def _publish_shard(ch: _Channel, x2: torch.Tensor) -> torch.Tensor:
+    """Copy this rank's shard into the channel's peer buffer."""
+    dst = ch.view(x2.numel()).view_as(x2)
+    dst.copy_(x2)
+    return dst
+
+
+def ag_gemm(owner, role, tp: TPContext, x_shard2: torch.Tensor, seq: int, w: torch.Tensor, w_mn: bool, epi: int,
+            **kw):
+    """[tokens, N] = AG_tokens(x_shard) . op(w)^T (gather mode, operand A rows).
+    Extra keywords (bias, aux, targets, ce_col0, ce_valid) go to the kernel."""
+    ch = channel(owner, role, tp, x_shard2.numel() * 2, x_shard2.device)
+    shard = _publish_shard(ch, x_shard2)
+    tokens = x_shard2.shape[0] * tp.world
+    n = w.shape[1] if w_mn else w.shape[0]
+    return native.lib().tp_gemm(
+        shard, False, w, w_mn, tokens, n, x_shard2.shape[1], epi, MODE_GATHER_A, ch.buf.ptrs, ch.flags.ptrs, ch.done,
+        tp.rank, seq, ch.next_epoch(), **kw,
+    )
+
+
+def gemm_rs(owner, role, tp: TPContext, a2: torch.Tensor, seq: int, w: torch.Tensor, w_mn: bool,
+            bias=None, resid2=None) -> torch.Tensor:
+    """[tokens/tp, N] = RS_tokens(a . op(w)^T) + bias + resid (scatter mode + slot reduction)."""
+    tokens = a2.shape[0]
+    n = w.shape[1] if w_mn else w.shape[0]
+    rows = tokens // tp.world
+    ch = channel(owner, role, tp, tokens * n * 2, a2.device)
+    lib = native.lib()
+    epoch = ch.next_epoch()
+    lib.tp_gemm(a2, False, w, w_mn, tokens, n, a2.shape[1], EPI_STORE, MODE_SCATTER, ch.buf.ptrs, ch.flags.ptrs,
+                ch.done, tp.rank, seq, epoch)
+    recv = ch.view(tokens * n).view(tp.world, rows, n)
+    return lib.tp_reduce(recv, tp.world, bias, resid2, ch.flags.ptrs, ch.done, tp.rank, epoch)
+
+
+def allgather_rows(owner, role, tp: TPContext, shard2: torch.Tensor, seq: int) -> torch.Tensor:
+    """Sequence shards [tokens/tp, N] of every rank -> full [tokens, N]."""
+    ch = channel(owner, role, tp, shard2.numel() * 2, shard2.device)
+    _publish_shard(ch, shard2)
+    return native.lib().tp_allgather(ch.buf.ptrs, shard2.shape[0], shard2.shape[1], seq, ch.flags.ptrs, ch.done,
+                                     tp.rank, ch.next_epoch(), shard2)
+
+
+def dw_gather_b(owner, role, tp: TPContext, dy2: torch.Tensor, x_shard2: torch.Tensor, seq: int, split: bool = True):
+    """dW [N_out, C] = dy^T . AG_tokens(x_shard): B gathered along K."""
+    ch = channel(owner, role, tp, x_shard2.numel() * 2, x_shard2.device)
+    shard = _publish_shard(ch, x_shard2)
+    tokens = dy2.shape[0]
+    res = native.lib().tp_gemm(
+        dy2, True, shard, True, dy2.shape[1], x_shard2.shape[1], tokens, EPI_PARTIAL_F32 if split else EPI_STORE,
+        MODE_GATHER_B, ch.buf.ptrs, ch.flags.ptrs, ch.done, tp.rank, seq, ch.next_epoch(),
+    )
+    return native.lib().splitk_reduce(res[0]) if split else res[0]
+
+
+def dw_gather_a(owner, role, tp: TPContext, dy_shard2: torch.Tensor, x2: torch.Tensor, seq: int):
+    """dW [N_out, K] = AG_tokens(dy_shard)^T . x: A gathered along K."""
+    ch = channel(owner, role, tp, dy_shard2.numel() * 2, dy_shard2.device)
+    shard = _publish_shard(ch, dy_shard2)
+    tokens = x2.shape[0]
+    res = native.lib().tp_gemm(
+        shard, True, x2, True, dy_shard2.shape[1], x2.shape[1], tokens, EPI_PARTIAL_F32, MODE_GATHER_A, ch.buf.ptrs,
+        ch.flags.ptrs, ch.done, tp.rank, seq, ch.next_epoch(),
+    )
+    return native.lib().splitk_reduce(res[0])
+
+
+# ---------------------------------------------------------------------- layers
+class _ColumnTP(torch.autograd.Function):
+    """Column-parallel linear under TP. sequence mode: x [B, T/tp, C] -> y
+    [B, T, N/tp] via AG+GEMM; replicated: x [B, T, C] -> y (no forward comm)."""
+
+    @staticmethod
+    def forward(ctx, x, w, b, tp, mode):
+        B, t = x.shape[0], x.shape[1]
+        x2 = _flat(x.contiguous())
+        if mode == "sequence":
+            seq = t * tp.world
+            y = ag_gemm(id(w), "col.fwd", tp, x2, seq, w, False, EPI_BIAS if b is not None else EPI_STORE, bias=b)[0]
+        else:
+            seq = t
+            y = gemm(x2, False, w, False, EPI_BIAS if b is not None else EPI_STORE, bias=b)
+        ctx.save_for_backward(x2, w)
+        ctx.meta = (tp, mode, seq, b is not None, x.shape, id(w))
+        return y.view(B, seq, w.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, w = ctx.saved_tensors
+        tp, mode, seq, has_b, xshape, k = ctx.meta
+        dy2 = _flat(dy.contiguous())
+        db = bias_grad(dy2) if has_b else None
+        if mode == "sequence":
+            dx = gemm_rs(k, "col.bwd.rs", tp, dy2, seq, w, True).view(xshape)
+            dw = dw_gather_b(k, "col.bwd.x", tp, dy2, x2, seq)
+        else:
+            dx_shard = gemm_rs(k, "col.bwd.rs", tp, dy2, seq, w, True)
+            dx = allgather_rows(k, "col.bwd.ag", tp, dx_shard, seq).view(xshape)
+            dw = weight_grad(dy2, x2)
+        return dx, dw, db, None, None
+
+
+class _RowTP(torch.autograd.Function):
+    """Row-parallel linear under TP: y = exit(x W^T) + bias (+ residual).
+    sequence mode: GEMM + reduce-scatter -> [B, T/tp, N]; replicated: GEMM +
+    reduce-scatter + all-gather -> [B, T, N]."""
+
+    @staticmethod
+    def forward(ctx, x, w, b, residual, tp, mode):
+        B, T = x.shape[0], x.shape[1]
+        x2 = _flat(x.contiguous())
+        rows = x2.shape[0] // tp.world
+        if mode == "sequence":
+            r2 = _flat(residual.contiguous()) if residual is not None else None
+            y = gemm_rs(id(w), "row.fwd.rs", tp, x2, T, w, False, bias=b, resid2=r2).view(B, T // tp.world, w.shape[0])
+        else:
+            r2 = None
+            if residual is not None:
+                tl = T // tp.world
+                r2 = _flat(residual[:, tp.rank * tl : (tp.rank + 1) * tl].contiguous())
+            shard = gemm_rs(id(w), "row.fwd.rs", tp, x2, T, w, False, bias=b, resid2=r2)
+            y = allgather_rows(id(w), "row.fwd.ag", tp, shard, T).view(B, T, w.shape[0])
+        ctx.save_for_backward(x2, w)
+        ctx.meta = (tp, mode, T, b is not None, residual is not None, x.shape, id(w))
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, w = ctx.saved_tensors
+        tp, mode, T, has_b, has_res, xshape, k = ctx.meta
+        dres = dy if has_res else None
+        dy2 = _flat(dy.contiguous())
+        db = bias_grad(dy2) if has_b else None  # sequence mode: partial, summed by finalize_grads
+        if mode == "sequence":
+            dx = ag_gemm(k, "row.bwd.dx", tp, dy2, T, w, True, EPI_STORE)[0].view(xshape)
+            dw = dw_gather_a(k, "row.bwd.dw", tp, dy2, x2, T)
+        else:
+            dx = gemm(dy2, False, w, True, EPI_STORE).view(xshape)
+            dw = weight_grad(dy2, x2)
+        return dx, dw, db, dres, None, None
+
+
+class _MLPTP(torch.autograd.Function):
+    """c_proj(gelu(c_fc(x))) + residual under TP with sequence parallelism:
+    AG+GEMM(+bias+GELU) then GEMM+RS(+bias+residual); backward mirrors it
+    with dGELU in the epilogue of the gathered c_proj dX GEMM."""
+
+    @staticmethod
+    def forward(ctx, x, w1, b1, w2, b2, residual, tp):
+        B, tl = x.shape[0], x.shape[1]
+        T = tl * tp.world
+        x2 = _flat(x.contiguous())
+        res = ag_gemm(id(w1), "mlp.fc.fwd", tp, x2, T, w1, False, EPI_BIAS_GELU, bias=b1)
+        h, pre = res[0], res[1]
+        r2 = _flat(residual.contiguous()) if residual is not None else None
+        y = gemm_rs(id(w2), "mlp.proj.fwd", tp, h, T, w2, False, bias=b2, resid2=r2).view(B, tl, w2.shape[0])
+        ctx.save_for_backward(x2, w1, pre, h, w2)
+        ctx.meta = (tp, T, b1 is not None, b2 is not None, residual is not None, x.shape, id(w1), id(w2))
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, w1, pre, h, w2 = ctx.saved_tensors
+        tp, T, has_b1, has_b2, has_res, xshape, k1, k2 = ctx.meta
+        dres = dy if has_res else None
+        dy2 = _flat(dy.contiguous())
+        db2 = bias_grad(dy2) if has_b2 else None  # partial over the sequence shard
+        dpre = ag_gemm(k2, "mlp.proj.bwd.dx", tp, dy2, T, w2, True, EPI_DGELU, aux=pre)[0]
+        dw2 = dw_gather_a(k2, "mlp.proj.bwd.dw", tp, dy2, h, T)
+        dx = gemm_rs(k1, "mlp.fc.bwd.rs", tp, dpre, T, w1, True).view(xshape)
+        dw1 = dw_gather_b(k1, "mlp.fc.bwd.x", tp, dpre, x2, T)
+        db1 = bias_grad(dpre) if has_b1 else None
+        return dx, dw1, db1, dw2, db2, dres, None
+
+
+def column_parallel(x, w, b, tp, mode):
+    return _ColumnTP.apply(x, w, b, tp, mode)
+
+
+def row_parallel(x, w, b, residual, tp, mode):
+    return _RowTP.apply(x, w, b, residual, tp, mode)
+
+
+def mlp_sequence_parallel(x, w1, b1, w2, b2, residual, tp):
+    return _MLPTP.apply(x, w1, b1, w2, b2, residual, tp)
+
+
+def usable(tp: TPContext, seq: int) -> bool:
+    """The fused kernels need sequence shards of a multiple of 128 tokens."""
+    return tp.enabled and tp.world <= 8 and seq % tp.world == 0 and (seq // tp.world) % 128 == 0

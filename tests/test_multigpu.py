@@ -31,3 +31,8 @@ def test_fused_dp_adam_2gpu():
 
 def test_tp_suite_2gpu_nccl():
     _torchrun(2, "tests/suites/tp_suite.py", "--sp", "--vp", "--device", "cuda")
+
+
+@pytest.mark.parametrize("sp", [True, False])
+def test_tp_fused_2gpu(sp):
+    _torchrun(2, "tests/suites/tp_fused_suite.py", *(["--sp"] if sp else []))
