@@ -71,7 +71,17 @@ static void launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
     configured[dev] = true;
   }
   static const PeerArgs none{};
-  kern<<<grid, kGemmThreads, smem, st>>>(ta, tb, to, tx, p, pa ? *pa : none);
+  if constexpr (GATHER == 1 && !A_MN) {
+    // CTAs wait on each other's copies: launch cooperatively so that every
+    // CTA of the grid is resident at once (one per SM).
+    const PeerArgs& pr = *pa;
+    void* args[] = {const_cast<CUtensorMap*>(&ta), const_cast<CUtensorMap*>(&tb), const_cast<CUtensorMap*>(&to),
+                    const_cast<CUtensorMap*>(&tx), const_cast<GemmParams*>(&p), const_cast<PeerArgs*>(&pr)};
+    C10_CUDA_CHECK(cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(kern), dim3(grid), dim3(kGemmThreads), args,
+                                               smem, st));
+  } else {
+    kern<<<grid, kGemmThreads, smem, st>>>(ta, tb, to, tx, p, pa ? *pa : none);
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -407,7 +417,8 @@ std::vector<at::Tensor> tp_gemm(const at::Tensor& A, bool a_mn, const at::Tensor
                                 const std::vector<int64_t>& flags, const at::Tensor& done, int64_t rank, int64_t seq,
                                 int64_t epoch, int64_t splits, const c10::optional<at::Tensor>& bias,
                                 const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& aux_out,
-                                const c10::optional<at::Tensor>& targets, int64_t ce_col0, int64_t ce_valid) {
+                                const c10::optional<at::Tensor>& targets, int64_t ce_col0, int64_t ce_valid,
+                                const c10::optional<at::Tensor>& gath, const c10::optional<at::Tensor>& arrive) {
   check_bf16_2d(A, "A");
   check_bf16_2d(B, "B");
   c10::cuda::CUDAGuard g(A.device());
@@ -444,6 +455,20 @@ std::vector<at::Tensor> tp_gemm(const at::Tensor& A, bool a_mn, const at::Tensor
     for (int r = 0; r < tp; ++r)
       pa.gather[r] = make_tmap_bf16(reinterpret_cast<void*>(peers[r]), G.size(1), G.size(0), G.stride(0), 64,
                                     g_mn ? 64 : kBM);
+    if (mode == 1 && !a_mn) {
+      // rows gathered through the local gather buffer (one NVLink crossing per byte)
+      TORCH_CHECK(gath.has_value() && arrive.has_value(), "tp_gemm: row gather needs gath and arrive buffers");
+      TORCH_CHECK(gath->is_contiguous() && gath->size(0) == M && gath->size(1) == K && gath->scalar_type() == at::kBFloat16,
+                  "tp_gemm: gath must be a contiguous bf16 [M, K] tensor");
+      TORCH_CHECK(A.is_contiguous() && K % 64 == 0, "tp_gemm: row gather needs a contiguous shard and K % 64 == 0");
+      TORCH_CHECK(arrive->scalar_type() == at::kInt && arrive->numel() >= (M + kBM - 1) / kBM, "tp_gemm: arrive");
+      for (int r = 0; r < tp; ++r) pa.shard[r] = reinterpret_cast<const __nv_bfloat16*>(peers[r]);
+      pa.shard_ld = static_cast<int>(K);
+      pa.gath = reinterpret_cast<__nv_bfloat16*>(gath->data_ptr());
+      pa.arrive = reinterpret_cast<unsigned int*>(arrive->data_ptr<int32_t>());
+      pa.kchunks = static_cast<int>(K / 64);
+      pa.gath_map = make_tmap_bf16(gath->data_ptr(), K, M, K, 64, kBM);
+    }
   } else {
     for (int r = 0; r < tp; ++r)
       pa.scatter[r] = make_tmap_bf16(reinterpret_cast<void*>(peers[r]), N, static_cast<uint64_t>(tp) * rows_local, N,
@@ -539,5 +564,5 @@ void register_gemm(pybind11::module& m) {
         py::arg("epi"), py::arg("mode"), py::arg("peers"), py::arg("flags"), py::arg("done"), py::arg("rank"),
         py::arg("seq"), py::arg("epoch"), py::arg("splits") = 0, py::arg("bias") = py::none(),
         py::arg("aux") = py::none(), py::arg("aux_out") = py::none(), py::arg("targets") = py::none(),
-        py::arg("ce_col0") = 0, py::arg("ce_valid") = 0);
+        py::arg("ce_col0") = 0, py::arg("ce_valid") = 0, py::arg("gath") = py::none(), py::arg("arrive") = py::none());
 }

@@ -101,7 +101,47 @@ struct PeerArgs {
   int seq_local;   // T / tp
   int rows_local;  // B * T / tp (rows of one receive slot)
   uint32_t epoch;
+  // Gather mode with a K-major operand (rows gathered): remote shards are
+  // copied ONCE into a local gather buffer by a copier warp in every CTA, so
+  // each remote byte crosses NVLink a single time; tiles of this rank's own
+  // shard are computed first while the copies are in flight.
+  const __nv_bfloat16* shard[kMaxPeers];  // each rank's shard (rows_local x K)
+  int shard_ld;                            // row stride (elements) of shards and gather buffer
+  __nv_bfloat16* gath;                     // local gather buffer [tokens, K]
+  unsigned int* arrive;                    // per 128-row block: copied 64-column chunks (monotonic)
+  int kchunks;                             // 64-column chunks per row block
+  CUtensorMap gath_map;                    // TMA map over gath (box 64 x 128)
 };
+
+// Row-block processing order of the gathered GEMM: this rank's own shard
+// first, then the shards of rank+1, rank+2, ... (the order their copies are
+// issued in). Logical index i -> global 128-row block.
+__device__ __forceinline__ int gather_mblock(const PeerArgs& pa, int i, int num_m) {
+  const int per_seg = pa.seq_local / 128;     // row blocks per (batch row, rank)
+  const int seg_blocks = pa.seq / 128;        // row blocks per batch row
+  const int per_src = (num_m / seg_blocks) * per_seg;
+  const int s = i / per_src, j = i - s * per_src;
+  const int src = (pa.rank + s) % pa.tp;
+  const int b = j / per_seg, tb = j - b * per_seg;
+  return b * seg_blocks + src * per_seg + tb;
+}
+
+// Output tile index -> (row block, column block). Plain GEMMs walk rows
+// fastest. The row-gathered GEMM goes source by source (all of this rank's
+// own tiles, over every column block, before any tile that needs a copied
+// block), rows fastest inside a source.
+template <bool ROW_GATHER>
+__device__ __forceinline__ void tile_coords(const PeerArgs& pa, int t, int num_m, int num_n, int& m_blk, int& n_blk) {
+  if (ROW_GATHER) {
+    const int per_src = num_m / pa.tp;
+    const int s = t / (per_src * num_n), r = t - s * per_src * num_n;
+    n_blk = r / per_src;
+    m_blk = gather_mblock(pa, s * per_src + (r - n_blk * per_src), num_m);
+  } else {
+    m_blk = t % num_m;
+    n_blk = t / num_m;
+  }
+}
 
 // Global token index -> (owning rank, row in the owner's local shard).
 __device__ __forceinline__ void token_owner(const PeerArgs& pa, int tok, int& src, int& local) {
@@ -123,7 +163,7 @@ __device__ __forceinline__ bool peer_wait_all(const PeerArgs& pa, int kind, uint
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kGemmThreads = 192;
+constexpr int kGemmThreads = 224;  // producer, MMA, 4 epilogue warps, copier (gather mode)
 constexpr int kEpiChunk = 64;                        // columns per epilogue chunk
 constexpr int kStageTileBytes = 32 * kEpiChunk * 2;  // one 32x64 bf16 staging tile
 
@@ -185,6 +225,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                      GemmParams p, const __grid_constant__ PeerArgs pa) {
   using Cfg = GemmCfg<BN>;
   constexpr int S = Cfg::kStages;
+  constexpr bool kRowGather = (GATHER == 1 && !A_MN);  // rows of A gathered via the copier
   static_assert(!(SCATTER && (EPI == kEpiPartialF32 || EPI == kEpiAccumF32 || EPI == kEpiBiasGelu ||
                               EPI == kEpiCEStats)),
                 "scatter mode takes a plain bf16 output");
@@ -258,10 +299,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
         const int tile = u % num_tiles;
         const int split = u / num_tiles;
-        const int m0 = (tile % num_m) * kBM;
-        const int n0 = (tile / num_m) * BN;
+        int mb_, nb_;
+        tile_coords<kRowGather>(pa, tile, num_m, num_n, mb_, nb_);
+        const int m0 = mb_ * kBM;
+        const int n0 = nb_ * BN;
         const int kb0 = split * p.k_blocks_per_split;
         const int kb1 = min(kb0 + p.k_blocks_per_split, k_blocks_total);
+        const CUtensorMap* rowA = &tmA;
+        int row_a = m0;
+        if (kRowGather) {
+          // Own rows straight from the local shard; remote rows from the
+          // gather buffer once the copier warps have landed all of them.
+          int src, local;
+          token_owner(pa, m0, src, local);
+          if (src == pa.rank) {
+            rowA = &pa.gather[pa.rank];
+            row_a = local;
+          } else {
+            const unsigned int need = pa.epoch * static_cast<unsigned int>(pa.kchunks);
+            if (!flag_wait_geq(pa.arrive + m0 / kBM, need, p.status, kTimeoutPeer)) {
+              ok = false;
+              break;
+            }
+            fence_proxy_async_global();
+            rowA = &pa.gath_map;
+          }
+        }
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, p.status, kTimeoutSmemEmpty)) {
             ok = false;
@@ -275,7 +338,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const CUtensorMap* mapA = &tmA;
           const CUtensorMap* mapB = &tmB;
           int a_m = m0, a_k = k0, b_n = n0, b_k = k0;
-          if (GATHER == 1) {
+          if (kRowGather) {
+            mapA = rowA;
+            a_m = row_a;
+          } else if (GATHER == 1) {
             mapA = A_MN ? source(k0, a_k) : source(m0, a_m);
             if (mapA == nullptr) {
               ok = false;
@@ -356,6 +422,48 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
     __syncwarp();
+  } else if (warp >= 6) {
+    // ------------------------------------------------------------ copier
+    // Gather mode: pull every remote row block of A into the local gather
+    // buffer once, source by source in processing order, 64-column chunks
+    // spread over the CTAs; each landed chunk bumps the block's counter.
+    if (kRowGather) {
+      const int per_src = num_m / pa.tp;
+      const int total = (pa.tp - 1) * per_src * pa.kchunks;
+      uint32_t ready = 0;
+      for (int c = blockIdx.x; c < total; c += gridDim.x) {
+        const int mb = gather_mblock(pa, per_src + c / pa.kchunks, num_m);  // skip own blocks
+        const int kc = c % pa.kchunks;
+        int src, local;
+        token_owner(pa, mb * kBM, src, local);
+        if (!(ready & (1u << src))) {
+          int okr = 1;
+          if (lane == 0)
+            okr = flag_wait_geq(pa.flags[pa.rank] + kGReady * kMaxPeers + src, pa.epoch, p.status, kTimeoutPeer);
+          if (!__shfl_sync(0xffffffff, okr, 0)) break;
+          ready |= 1u << src;
+        }
+        const __nv_bfloat16* s = pa.shard[src] + static_cast<size_t>(local) * pa.shard_ld + kc * 64;
+        __nv_bfloat16* d = pa.gath + static_cast<size_t>(mb) * kBM * pa.shard_ld + kc * 64;
+#pragma unroll 1
+        for (int base = 0; base < kBM * 8; base += 32 * 16) {  // 16 loads in flight per lane
+          uint4 t[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int v = base + j * 32 + lane;
+            t[j] = *reinterpret_cast<const uint4*>(s + static_cast<size_t>(v >> 3) * pa.shard_ld + (v & 7) * 8);
+          }
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int v = base + j * 32 + lane;
+            *reinterpret_cast<uint4*>(d + static_cast<size_t>(v >> 3) * pa.shard_ld + (v & 7) * 8) = t[j];
+          }
+        }
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) atomicAdd(pa.arrive + mb, 1u);
+      }
+    }
   } else {
     // ------------------------------------------------------------ epilogue
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
@@ -368,8 +476,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++iter) {
       const int tile = u % num_tiles;
       const int split = u / num_tiles;
-      const int m_blk = tile % num_m;
-      const int n_blk = tile / num_m;
+      int m_blk, n_blk;
+      tile_coords<kRowGather>(pa, tile, num_m, num_n, m_blk, n_blk);
       const int m0 = m_blk * kBM;
       const int n0 = n_blk * BN;
       const int acc = iter & 1;

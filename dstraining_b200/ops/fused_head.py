@@ -40,11 +40,11 @@ class _FusedHeadCE(torch.autograd.Function):
         seq = x.shape[1] * tp.world if (seq_parallel and tp.enabled) else x.shape[1]
         fused_sp = seq_parallel and tp.enabled and tp_fused.usable(tp, seq)
         if fused_sp:
-            x2 = x.reshape(-1, x.shape[-1]).contiguous()  # this rank's sequence shard
-            logits, tmax, tsum, tgt = tp_fused.ag_gemm(
-                id(w), "head.fwd", tp, x2, seq, w, False, tp_fused.EPI_CE_STATS, targets=tg, ce_col0=col0,
+            xs = x.reshape(-1, x.shape[-1]).contiguous()  # this rank's sequence shard
+            (logits, tmax, tsum, tgt), x2 = tp_fused.ag_gemm(
+                id(w), "head.fwd", tp, xs, seq, w, False, tp_fused.EPI_CE_STATS, targets=tg, ce_col0=col0,
                 ce_valid=valid,
-            )
+            )  # x2: the gathered input, kept for dW
         else:
             if seq_parallel and tp.enabled:
                 x = all_gather_dim(x, tp, 1)
@@ -69,7 +69,7 @@ class _FusedHeadCE(torch.autograd.Function):
         lib.ce_grad_inplace(logits, lse.contiguous(), tg, col0, valid, g.float().reshape(1).contiguous(), 1.0 / n)
         if fused_sp:
             dx = tp_fused.gemm_rs(k, "head.bwd.rs", tp, logits, seq, w, True).view(xshape)
-            dw = tp_fused.dw_gather_b(k, "head.bwd.x", tp, logits, x2, seq, split=False)
+            dw = gemm(logits, True, x2, True, EPI_STORE)
             return dx, dw, None, None, None, None
         dx = gemm(logits, False, w, True, EPI_STORE).view(xshape)
         dw = gemm(logits, True, x2, True, EPI_STORE)

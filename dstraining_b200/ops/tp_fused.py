@@ -86,16 +86,30 @@ def _publish_shard(ch: _Channel, x2: torch.Tensor) -> torch.Tensor:
 
 def ag_gemm(owner, role, tp: TPContext, x_shard2: torch.Tensor, seq: int, w: torch.Tensor, w_mn: bool, epi: int,
             **kw):
-    """[tokens, N] = AG_tokens(x_shard) . op(w)^T (gather mode, operand A rows).
-    Extra keywords (bias, aux, targets, ce_col0, ce_valid) go to the kernel."""
+    """AG_tokens(x_shard) . op(w)^T (gather mode, rows of operand A).
+
+    Returns ``(results, gathered)``: the kernel's outputs (``[tokens, N]``
+    first) and the gathered ``[tokens, K]`` input, which the kernel assembles
+    locally while it computes (each remote byte crosses NVLink once) and which
+    backward reuses. Extra keywords (bias, aux, targets, ce_col0, ce_valid)
+    go to the kernel."""
     ch = channel(owner, role, tp, x_shard2.numel() * 2, x_shard2.device)
     shard = _publish_shard(ch, x_shard2)
     tokens = x_shard2.shape[0] * tp.world
     n = w.shape[1] if w_mn else w.shape[0]
-    return native.lib().tp_gemm(
+    if getattr(ch, "arrive", None) is None:
+        ch.arrive = torch.zeros(-(-tokens // 128), dtype=torch.int32, device=x_shard2.device)
+    gathered = torch.empty(tokens, x_shard2.shape[1], dtype=x_shard2.dtype, device=x_shard2.device)
+    res = native.lib().tp_gemm(
         shard, False, w, w_mn, tokens, n, x_shard2.shape[1], epi, MODE_GATHER_A, ch.buf.ptrs, ch.flags.ptrs, ch.done,
-        tp.rank, seq, ch.next_epoch(), **kw,
+        tp.rank, seq, ch.next_epoch(), gath=gathered, arrive=ch.arrive, **kw,
     )
+    # Rows of this rank's own shard are read in place by the kernel; fill
+    # them into the gathered copy for backward.
+    t_loc = seq // tp.world
+    g3 = gathered.view(-1, seq, gathered.shape[1])
+    g3[:, tp.rank * t_loc : (tp.rank + 1) * t_loc].copy_(x_shard2.view(-1, t_loc, x_shard2.shape[1]))
+    return res, gathered
 
 
 def gemm_rs(owner, role, tp: TPContext, a2: torch.Tensor, seq: int, w: torch.Tensor, w_mn: bool,
@@ -156,27 +170,28 @@ class _ColumnTP(torch.autograd.Function):
         x2 = _flat(x.contiguous())
         if mode == "sequence":
             seq = t * tp.world
-            y = ag_gemm(id(w), "col.fwd", tp, x2, seq, w, False, EPI_BIAS if b is not None else EPI_STORE, bias=b)[0]
+            res, xg = ag_gemm(id(w), "col.fwd", tp, x2, seq, w, False, EPI_BIAS if b is not None else EPI_STORE, bias=b)
+            y = res[0]
         else:
             seq = t
             y = gemm(x2, False, w, False, EPI_BIAS if b is not None else EPI_STORE, bias=b)
-        ctx.save_for_backward(x2, w)
+            xg = x2
+        ctx.save_for_backward(xg, w)  # the (gathered) input, for dW
         ctx.meta = (tp, mode, seq, b is not None, x.shape, id(w))
         return y.view(B, seq, w.shape[0])
 
     @staticmethod
     def backward(ctx, dy):
-        x2, w = ctx.saved_tensors
+        xg, w = ctx.saved_tensors
         tp, mode, seq, has_b, xshape, k = ctx.meta
         dy2 = _flat(dy.contiguous())
         db = bias_grad(dy2) if has_b else None
         if mode == "sequence":
             dx = gemm_rs(k, "col.bwd.rs", tp, dy2, seq, w, True).view(xshape)
-            dw = dw_gather_b(k, "col.bwd.x", tp, dy2, x2, seq)
         else:
             dx_shard = gemm_rs(k, "col.bwd.rs", tp, dy2, seq, w, True)
             dx = allgather_rows(k, "col.bwd.ag", tp, dx_shard, seq).view(xshape)
-            dw = weight_grad(dy2, x2)
+        dw = weight_grad(dy2, xg)
         return dx, dw, db, None, None
 
 
@@ -212,8 +227,9 @@ class _RowTP(torch.autograd.Function):
         dy2 = _flat(dy.contiguous())
         db = bias_grad(dy2) if has_b else None  # sequence mode: partial, summed by finalize_grads
         if mode == "sequence":
-            dx = ag_gemm(k, "row.bwd.dx", tp, dy2, T, w, True, EPI_STORE)[0].view(xshape)
-            dw = dw_gather_a(k, "row.bwd.dw", tp, dy2, x2, T)
+            res, dyg = ag_gemm(k, "row.bwd.dx", tp, dy2, T, w, True, EPI_STORE)
+            dx = res[0].view(xshape)
+            dw = weight_grad(dyg, x2)
         else:
             dx = gemm(dy2, False, w, True, EPI_STORE).view(xshape)
             dw = weight_grad(dy2, x2)
@@ -230,25 +246,26 @@ class _MLPTP(torch.autograd.Function):
         B, tl = x.shape[0], x.shape[1]
         T = tl * tp.world
         x2 = _flat(x.contiguous())
-        res = ag_gemm(id(w1), "mlp.fc.fwd", tp, x2, T, w1, False, EPI_BIAS_GELU, bias=b1)
+        res, xg = ag_gemm(id(w1), "mlp.fc.fwd", tp, x2, T, w1, False, EPI_BIAS_GELU, bias=b1)
         h, pre = res[0], res[1]
         r2 = _flat(residual.contiguous()) if residual is not None else None
         y = gemm_rs(id(w2), "mlp.proj.fwd", tp, h, T, w2, False, bias=b2, resid2=r2).view(B, tl, w2.shape[0])
-        ctx.save_for_backward(x2, w1, pre, h, w2)
+        ctx.save_for_backward(xg, w1, pre, h, w2)
         ctx.meta = (tp, T, b1 is not None, b2 is not None, residual is not None, x.shape, id(w1), id(w2))
         return y
 
     @staticmethod
     def backward(ctx, dy):
-        x2, w1, pre, h, w2 = ctx.saved_tensors
+        xg, w1, pre, h, w2 = ctx.saved_tensors
         tp, T, has_b1, has_b2, has_res, xshape, k1, k2 = ctx.meta
         dres = dy if has_res else None
         dy2 = _flat(dy.contiguous())
         db2 = bias_grad(dy2) if has_b2 else None  # partial over the sequence shard
-        dpre = ag_gemm(k2, "mlp.proj.bwd.dx", tp, dy2, T, w2, True, EPI_DGELU, aux=pre)[0]
-        dw2 = dw_gather_a(k2, "mlp.proj.bwd.dw", tp, dy2, h, T)
+        res, dyg = ag_gemm(k2, "mlp.proj.bwd.dx", tp, dy2, T, w2, True, EPI_DGELU, aux=pre)
+        dpre = res[0]
+        dw2 = weight_grad(dyg, h)
         dx = gemm_rs(k1, "mlp.fc.bwd.rs", tp, dpre, T, w1, True).view(xshape)
-        dw1 = dw_gather_b(k1, "mlp.fc.bwd.x", tp, dpre, x2, T)
+        dw1 = weight_grad(dpre, xg)
         db1 = bias_grad(dpre) if has_b1 else None
         return dx, dw1, db1, dw2, db2, dres, None
 
