@@ -502,6 +502,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           my_bias[2 * lane + 1] = bv.y;
           __syncwarp();
         }
+        // Auxiliary operand (residual / pre-activation) of this 64-column
+        // chunk: issue the row's loads now so they overlap the TMEM reads.
+        uint4 auxv[8];
+        if (EPI == kEpiBiasResid || EPI == kEpiDGelu) {
+          const int nvalid = max(0, min(kEpiChunk, p.N - col0));
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            auxv[q] = make_uint4(0u, 0u, 0u, 0u);
+            if (row_ok && q * 8 < nvalid)
+              auxv[q] = *reinterpret_cast<const uint4*>(p.aux + static_cast<size_t>(row) * p.ld_aux + col0 + q * 8);
+          }
+        }
         uint8_t* tile_a = my_stage + (chunk_count & 1) * kStageTileBytes;
         uint8_t* tile_b = my_stage + ((chunk_count & 1) ^ 1) * kStageTileBytes;
         if (!kF32Out) {
@@ -557,16 +569,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               const float x = __bfloat162float(__float2bfloat16_rn(v[i]));
               v[i] = gelu_tanh(x);
             }
-          } else if (EPI == kEpiBiasResid) {
-            float r[32];
-            if (row_ok) load_bf16x32(p.aux + static_cast<size_t>(row) * p.ld_aux + col, r, valid);
+          } else if (EPI == kEpiBiasResid || EPI == kEpiDGelu) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] += row_ok ? r[i] : 0.f;
-          } else if (EPI == kEpiDGelu) {
-            float x[32];
-            if (row_ok) load_bf16x32(p.aux + static_cast<size_t>(row) * p.ld_aux + col, x, valid);
+            for (int q = 0; q < 4; ++q) {
+              const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&auxv[half * 4 + q]);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] *= row_ok ? gelu_tanh_grad(x[i]) : 0.f;
+              for (int j = 0; j < 4; ++j) {
+                const float2 f = __bfloat1622float2(h2[j]);
+                if (EPI == kEpiBiasResid) {
+                  v[q * 8 + 2 * j] += f.x;
+                  v[q * 8 + 2 * j + 1] += f.y;
+                } else {
+                  v[q * 8 + 2 * j] *= gelu_tanh_grad(f.x);
+                  v[q * 8 + 2 * j + 1] *= gelu_tanh_grad(f.y);
+                }
+              }
+            }
           } else if (EPI == kEpiCEStats) {
             float cm = -INFINITY;
 #pragma unroll

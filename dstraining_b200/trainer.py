@@ -102,12 +102,14 @@ class Trainer:
         else:
             self.pipe = None
         self.fused_dp = (
-            args.bf16 and self.dp.enabled and not args.naive_dp and self.device.type == "cuda"
+            args.bf16 and not args.naive_dp and self.device.type == "cuda"
             and os.environ.get("DST_FUSED_DP", "1") != "0"
         )
         if self.fused_dp:
             # DP reduction + fp32-master Adam + parameter all-gather in one
-            # NVLink kernel per bucket (sharded optimizer state).
+            # NVLink kernel per bucket (sharded optimizer state). With a single
+            # replica the same kernel is the bucketed Adam update, launched on
+            # a side stream as backward finishes each bucket.
             self.opt = FusedDPAdam(
                 model, self.dp, lr=args.lr, bucket_bytes=int(args.bucket_mb * 1024 * 1024), overlap=self.pipe is None
             )

@@ -56,11 +56,17 @@ def _global_name(model: nn.Module, name: str) -> str:
 
 def _optimizer_state(opt, params):
     """Per-parameter fp32 state tensors: master weights and Adam moments when
-    the optimizer keeps them; ``step`` as a float."""
+    the optimizer keeps them; ``step`` as a float. Sharded optimizer state
+    (FusedDPAdam) is gathered over the DP group - collective."""
+    from ..optim.fused_dp import FusedDPAdam
     from ..optim.precision import MasterWeightOptimizer
 
     out = {}
     step = 0.0
+    if isinstance(opt, FusedDPAdam):
+        for name, p in params:
+            out[name] = opt.full_state(p)
+        return out, float(opt._step)
     if isinstance(opt, MasterWeightOptimizer):
         by_param = dict(zip([id(p) for p in opt.model_params], opt.master_params))
         for name, p in params:
@@ -175,6 +181,7 @@ class _Reader:
 def load(path: str, model: nn.Module, opt, tp) -> dict:
     """Load weights (and optimizer state when present) into this rank's
     model/optimizer, resharding as needed. Returns the manifest."""
+    from ..optim.fused_dp import FusedDPAdam
     from ..optim.precision import MasterWeightOptimizer
 
     rd = _Reader(path)
@@ -201,7 +208,18 @@ def load(path: str, model: nn.Module, opt, tp) -> dict:
             if w is None:
                 raise KeyError(f"checkpoint {path} has no tensor for {g}")
             p.copy_(w.to(p.dtype))
-            if isinstance(opt, MasterWeightOptimizer) and id(p) in masters:
+            if isinstance(opt, FusedDPAdam):
+                src = local(f"master/{g}", name, p)
+                ea, eas = local(f"exp_avg/{g}", name, p), local(f"exp_avg_sq/{g}", name, p)
+                zeros = torch.zeros(p.shape)
+                opt.load_full_state(
+                    p,
+                    src if src is not None else w.float(),
+                    ea if ea is not None else zeros,
+                    eas if eas is not None else zeros,
+                    int(opt_step),
+                )
+            elif isinstance(opt, MasterWeightOptimizer) and id(p) in masters:
                 m = masters[id(p)]
                 src = local(f"master/{g}", name, p)
                 m.copy_(src if src is not None else w.float())
