@@ -1,0 +1,168 @@
+"""Failure detection for multi-rank training (host side).
+
+Three layers, none of which needs a GPU fault to be exercised:
+
+* a short, configurable process-group timeout (``DST_PG_TIMEOUT_S``, set in
+  :func:`dstraining_b200.parallel.topology.init_distributed`): a collective
+  whose peer died or stalled ends with an error instead of waiting forever;
+* :class:`Heartbeat`: every rank publishes a timestamp into the rendezvous
+  store (the c10d store every rank already shares) every ``interval`` seconds
+  from a daemon thread;
+* :class:`Watchdog`: a daemon thread that reads every rank's heartbeat and,
+  when one is older than ``timeout`` (or a rank has posted a failure
+  record), reports it and by default terminates this process with exit code
+  3 - so a survivor does not sit in a collective until the much longer
+  process-group timeout, and the launcher sees the job fail.
+
+``report_failure(reason)`` lets a rank that catches an exception tell its
+peers before it exits. Device-side waits are bounded inside the kernels
+(status word, see ``read_status``); this module covers ranks.
+
+The reference has no failure handling (its only guard is
+``GradReducer.finish`` launching never-launched buckets, ``dst/dp.py:134-138``).
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+import threading
+import time
+from typing import Callable, List, Optional
+
+import torch.distributed as dist
+
+_PREFIX = "dst/health"
+
+
+def _store():
+    return dist.distributed_c10d._get_default_store()
+
+
+class PeerFailure(RuntimeError):
+    pass
+
+
+class Heartbeat:
+    """Publishes this rank's last *progress* time. The training loop calls
+    :meth:`tick` once per step; a daemon thread writes the latest tick into
+    the store every ``interval`` seconds (so a slow store never stalls the
+    step). A rank whose main loop hangs stops ticking; a rank that dies stops
+    publishing; either way its entry goes stale."""
+
+    def __init__(self, interval: float = 1.0):
+        self.interval = interval
+        self.rank = dist.get_rank()
+        self.last = time.time()
+        self._stop = threading.Event()
+        self._thread = threading.Thread(target=self._run, name="dst-heartbeat", daemon=True)
+        self.beat()
+
+    def tick(self) -> None:
+        self.last = time.time()
+
+    def beat(self) -> None:
+        _store().set(f"{_PREFIX}/hb/{self.rank}", repr(self.last))
+
+    def _run(self) -> None:
+        while not self._stop.wait(self.interval):
+            try:
+                self.beat()
+            except Exception:  # noqa: BLE001 - store gone: the job is ending
+                return
+
+    def start(self) -> "Heartbeat":
+        self._thread.start()
+        return self
+
+    def stop(self) -> None:
+        self._stop.set()
+
+
+def report_failure(reason: str) -> None:
+    """Tell every rank that this rank has failed (best effort)."""
+    try:
+        _store().set(f"{_PREFIX}/failed/{dist.get_rank()}", reason[:200])
+        _store().add(f"{_PREFIX}/nfailed", 1)
+    except Exception:  # noqa: BLE001
+        pass
+
+
+def stale_ranks(timeout: float, world: Optional[int] = None) -> List[int]:
+    """Ranks whose last heartbeat is older than ``timeout`` seconds (or that
+    never published one), plus ranks that reported a failure."""
+    store = _store()
+    world = dist.get_world_size() if world is None else world
+    now = time.time()
+    bad = []
+    failed = int(store.add(f"{_PREFIX}/nfailed", 0))
+    for r in range(world):
+        if failed:
+            try:
+                if store.check([f"{_PREFIX}/failed/{r}"]):
+                    bad.append(r)
+                    continue
+            except Exception:  # noqa: BLE001
+                pass
+        key = f"{_PREFIX}/hb/{r}"
+        try:
+            if not store.check([key]):
+                bad.append(r)
+                continue
+            t = float(store.get(key).decode())
+        except Exception:  # noqa: BLE001
+            bad.append(r)
+            continue
+        if now - t > timeout:
+            bad.append(r)
+    return bad
+
+
+class Watchdog:
+    """Polls peers' heartbeats; on a stale or failed peer calls ``on_failure``
+    (default: print and ``os._exit(3)``)."""
+
+    def __init__(self, timeout: float = 10.0, poll: float = 0.5, on_failure: Optional[Callable[[List[int]], None]] = None,
+                 grace: float = 5.0):
+        self.timeout = timeout
+        self.poll = poll
+        self.grace = grace
+        self.on_failure = on_failure or self._abort
+        self._stop = threading.Event()
+        self._thread = threading.Thread(target=self._run, name="dst-watchdog", daemon=True)
+        self.failed: List[int] = []
+
+    @staticmethod
+    def _abort(ranks: List[int]) -> None:
+        print(f"[dst watchdog] rank {dist.get_rank()}: peer rank(s) {ranks} stopped responding; aborting",
+              file=sys.stderr, flush=True)
+        os._exit(3)
+
+    def _run(self) -> None:
+        start = time.time()
+        while not self._stop.wait(self.poll):
+            if time.time() - start < self.grace:
+                continue  # let every rank publish its first heartbeat
+            try:
+                bad = stale_ranks(self.timeout)
+            except Exception:  # noqa: BLE001 - store unreachable: rank 0 (the store host) died
+                bad = [0]
+            bad = [r for r in bad if r != dist.get_rank()]
+            if bad:
+                self.failed = bad
+                self.on_failure(bad)
+                return
+
+    def start(self) -> "Watchdog":
+        self._thread.start()
+        return self
+
+    def stop(self) -> None:
+        self._stop.set()
+
+
+def start_monitoring(interval: float = 1.0, timeout: float = 10.0):
+    """Heartbeat + watchdog for this rank; returns both (call ``stop()``)."""
+    hb = Heartbeat(interval).start()
+    wd = Watchdog(timeout=timeout, poll=min(0.5, interval)).start()
+    return hb, wd

@@ -63,6 +63,8 @@ def add_args(p: argparse.ArgumentParser) -> argparse.ArgumentParser:
     p.add_argument("--ckpt-every", type=int, default=0, help="save every N steps (0: only at the end if --ckpt-dir)")
     p.add_argument("--resume", action="store_true", help="resume from the latest checkpoint in --ckpt-dir")
     p.add_argument("--jsonl", default=None, help="append per-step metrics (JSON lines) to this file")
+    p.add_argument("--heartbeat-timeout", type=float, default=0.0,
+                   help="abort when a peer makes no progress for this many seconds (0: off)")
     return p
 
 
@@ -129,6 +131,12 @@ class Trainer:
         self.tokens_per_step = args.batch * cfg.block_size * args.dp
         self.is_logger = self.pp.is_last and self.tp.rank == 0 and self.dp.rank == 0
         self.step_index = 0
+        self.heartbeat = self.watchdog = None
+        if getattr(args, "heartbeat_timeout", 0.0) and dist.is_initialized() and dist.get_world_size() > 1:
+            from .parallel.health import start_monitoring
+
+            hb_timeout = args.heartbeat_timeout
+            self.heartbeat, self.watchdog = start_monitoring(interval=min(1.0, hb_timeout / 4), timeout=hb_timeout)
 
     @property
     def n_params(self) -> int:
@@ -150,6 +158,8 @@ class Trainer:
         self.model.finalize_grads()
         self.opt.step()
         self.step_index += 1
+        if self.heartbeat is not None:
+            self.heartbeat.tick()
         return loss
 
     def step(self, idx: torch.Tensor, tgt: torch.Tensor) -> Optional[float]:

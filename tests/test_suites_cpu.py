@@ -81,7 +81,8 @@ def test_train_cli_all_axes_and_resume(tmp_path):
     env = dict(os.environ, CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="1")
     ck = str(tmp_path / "ck")
     common = ["--dp", "2", "--pp", "2", "--tp", "2", "--chunks", "2", "--sp", "--recompute", "--vp",
-              "--micro", "1", "--batch", "4", "--device", "cpu", "--ckpt-dir", ck, "--jsonl", str(tmp_path / "m.jsonl")]
+              "--micro", "1", "--batch", "4", "--device", "cpu", "--ckpt-dir", ck, "--jsonl", str(tmp_path / "m.jsonl"),
+              "--heartbeat-timeout", "120"]  # healthy job: the watchdog must not fire
     assert launch(8, [train, "--steps", "4", *common], timeout=540, env=env) == 0
     assert launch(8, [train, "--steps", "6", "--resume", *common], timeout=540, env=env) == 0
     lines = open(tmp_path / "m.jsonl").read().splitlines()
@@ -91,3 +92,20 @@ def test_train_cli_all_axes_and_resume(tmp_path):
 @pytest.mark.parametrize("n,args", [(2, ("--dp", "2")), (4, ("--dp", "2", "--tp", "2", "--sp")), (4, ("--dp", "4",))])
 def test_fused_dp_suite(n, args):
     run(n, "fused_dp_suite.py", *args)
+
+
+@pytest.mark.parametrize("mode", ["raise", "hang", "exit"])
+def test_failure_detection(mode, tmp_path):
+    """A rank fails on the host (raises, hangs, or exits); the job must end
+    with a non-zero status long before the process-group timeout, with the
+    survivors' watchdogs reporting the failure."""
+    import time
+
+    marker = str(tmp_path / "m")
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="1")
+    t0 = time.time()
+    rc = launch(3, [os.path.join(SUITES, "fault_suite.py"), "--mode", mode, "--victim", "1", "--marker", marker],
+                timeout=120, env=env)
+    assert rc != 0
+    assert time.time() - t0 < 60
+    assert any(os.path.exists(f"{marker}.{r}") for r in range(3)), "no rank detected the failure"

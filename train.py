@@ -28,6 +28,17 @@ from dstraining_b200.utils import checkpoint
 
 def main():
     args = add_args(argparse.ArgumentParser()).parse_args()
+    try:
+        run(args)
+    except Exception as e:  # tell the peers before dying, so they stop waiting
+        if dist.is_initialized():
+            from dstraining_b200.parallel.health import report_failure
+
+            report_failure(f"{type(e).__name__}: {e}")
+        raise
+
+
+def run(args):
     tr = Trainer(args)
     start_step = 0
     if args.resume and args.ckpt_dir:
