@@ -1,11 +1,23 @@
-"""Throughput benchmark: GPT-2 small (12L/768/12H, seq 1024, vocab 50304),
-pure data parallelism dp=N, bf16 with fp32 master weights, micro-batch 16
-per rank, 25 MB gradient buckets.
+"""Throughput benchmark on the BASELINE.json configs, ours vs the reference.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--config c2|c3|c4|c5] [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Configs (synthetic uniform-random token ids, random-init weights, bf16 with
+fp32 master weights, vocab 50304):
+
+* ``c2`` (default, the headline): GPT-2 small (12L/768/12H, seq 1024), pure
+  data parallelism dp=N, micro-batch 16 per rank, 25 MB gradient buckets.
+  Weak scaling.
+* ``c3``: tp=N with sequence parallelism, vocab-parallel CE and selective
+  attention recompute; 16L/2048/16H, seq 2048, batch 4. Strong scaling.
+* ``c4``: interleaved pipeline, v=2 chunks per rank, x tp=2 (N=8: pp4 x tp2;
+  N=4: pp2 x tp2; N=2: pp2); 32L/2048/16H, seq 2048, m=16 micro-batches of 2.
+* ``c5``: tp2 x pp2 x dp2 (N=8; N=4: tp2 x pp2; N=2: pp2), SP, 1F1B,
+  bucketed DP, vocab-parallel CE; 24L/2048/16H, seq 2048, global batch 64
+  in micro-batches of 2.
 
 For N > 1 launch one process per GPU:
-    python -m torch.distributed.run --nnodes=1 --nproc-per-node N \
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N \\
         --master-addr 127.0.0.1 --master-port P bench.py --gpus N ...
 
 Protocol: W untimed warm-up steps, then K steps timed on the device with
@@ -18,9 +30,10 @@ end to end through the public API (``Trainer.step``: pinned host batch ->
 device copy -> step -> loss read back), which is the ``e2e`` figure.
 
 ``--impl reference`` runs the unmodified reference package installed under
-``baseline/_ref`` through its own public API (its GPT, MasterWeightOptimizer,
-GradReducer and SyntheticShard), timed identically. Rank 0 prints one JSON
-line.
+``baseline/_ref`` through its own public API (its GPT / GPTStage,
+Pipeline1F1B, MasterWeightOptimizer, GradReducer and SyntheticShard,
+assembled as its ``train.py:60-125`` does), timed identically. Rank 0
+prints one JSON line.
 """
 
 from __future__ import annotations
@@ -33,17 +46,73 @@ import subprocess
 import sys
 import threading
 import time
+from dataclasses import dataclass
+from typing import Callable, Optional
 
 import torch
 import torch.distributed as dist
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-MODEL = dict(layers=12, heads=12, embd=768, block=1024, vocab=50304)
-MICRO = 16
-# Published reference numbers for GPT-2 124M (RTX 4090, docs/WRITEUP.md:311-312):
-# 1 GPU 41.6k tok/s, dp=2 bucketed 75.4k tok/s. No B200 numbers are published.
-PUBLISHED = {1: 41600.0, 2: 75400.0}
 REASONS = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+
+
+@dataclass
+class BenchConfig:
+    name: str
+    description: str
+    layers: int
+    heads: int
+    embd: int
+    block: int
+    batch: Callable[[dict], int]  # per-DP-replica batch for a layout
+    micro: int
+    layout: Callable[[int], Optional[dict]]  # n_gpus -> {tp, pp, dp, chunks} or None
+    sp: bool = False
+    vp: bool = True
+    recompute: bool = False
+    scaling: str = "strong"
+    vocab: int = 50304
+    published: Optional[dict] = None  # n_gpus -> the reference's published tok/s (other hardware)
+
+
+def _layout(tp=1, pp=1, dp=1, chunks=1):
+    return dict(tp=tp, pp=pp, dp=dp, chunks=chunks)
+
+
+CONFIGS = {
+    "c2": BenchConfig(
+        "c2", "GPT-2 small 12L/768/12H, d_ff 3072, seq 1024, vocab 50304 (BASELINE config 2)",
+        12, 12, 768, 1024, batch=lambda lay: 16, micro=16, layout=lambda n: _layout(dp=n), scaling="weak",
+        # Published reference numbers for GPT-2 124M (RTX 4090, docs/WRITEUP.md:311-312):
+        # 1 GPU 41.6k tok/s, dp=2 bucketed 75.4k tok/s. No B200 numbers are published.
+        published={1: 41600.0, 2: 75400.0},
+    ),
+    "c3": BenchConfig(
+        "c3", "16L/2048/16H, d_ff 8192, seq 2048, vocab 50304, tp=N + SP + vocab-parallel CE + recompute, "
+        "batch 4 (BASELINE config 3)",
+        16, 16, 2048, 2048, batch=lambda lay: 4, micro=4, layout=lambda n: _layout(tp=n), sp=True, recompute=True,
+    ),
+    "c4": BenchConfig(
+        "c4", "32L/2048/16H, d_ff 8192, seq 2048, vocab 50304, interleaved pipeline v=2 x tp, m=16 micro-batches "
+        "of 2 (BASELINE config 4)",
+        32, 16, 2048, 2048, batch=lambda lay: 32, micro=2,
+        layout=lambda n: {8: _layout(tp=2, pp=4, chunks=2), 4: _layout(tp=2, pp=2, chunks=2),
+                          2: _layout(pp=2, chunks=2)}.get(n),
+    ),
+    "c5": BenchConfig(
+        "c5", "24L/2048/16H (~1.3B), d_ff 8192, seq 2048, vocab 50304, tp x pp x dp + SP, 1F1B, bucketed DP, "
+        "vocab-parallel CE, global batch 64 in micro-batches of 2 (BASELINE config 5)",
+        24, 16, 2048, 2048, batch=lambda lay: 64 // lay["dp"], micro=2,
+        layout=lambda n: {8: _layout(tp=2, pp=2, dp=2), 4: _layout(tp=2, pp=2), 2: _layout(pp=2)}.get(n), sp=True,
+    ),
+}
+
+
+def parallelism_name(lay: dict) -> str:
+    parts = [f"{k}{lay[k]}" for k in ("tp", "pp", "dp") if lay[k] > 1]
+    if lay["chunks"] > 1:
+        parts.append(f"v{lay['chunks']}")
+    return "x".join(parts) or "single"
 
 
 class ClockSampler:
@@ -170,25 +239,37 @@ def count_launches(step_fn, ours_marker):
     return ours, other, top_other
 
 
+def final_loss(losses) -> float:
+    """The last step's loss from whichever ranks hold it (the last pipeline
+    stage), as a host float on every rank."""
+    last = losses[-1] if losses else None
+    x = float(last.detach().float().item()) if last is not None else float("-inf")
+    return max_over_ranks(x)
+
+
 # ---------------------------------------------------------------- our arm
-def run_ours(a, rank, world):
+def run_ours(a, cfg: BenchConfig, lay: dict, rank, world):
     sys.path.insert(0, HERE)
     from dstraining_b200.trainer import Trainer, add_args
 
     targs = add_args(argparse.ArgumentParser()).parse_args([])
-    targs.dp = world
+    targs.tp, targs.pp, targs.dp, targs.chunks = lay["tp"], lay["pp"], lay["dp"], lay["chunks"]
     targs.bf16 = True
-    targs.vp = True  # fused LM head + CE: the same loss as plain CE at tp=1
-    targs.layers, targs.heads, targs.embd = MODEL["layers"], MODEL["heads"], MODEL["embd"]
-    targs.block, targs.vocab = MODEL["block"], MODEL["vocab"]
-    targs.batch = MICRO
+    targs.vp = cfg.vp  # at tp=1 this is the fused LM head + CE: the same loss as plain CE
+    targs.sp = cfg.sp and lay["tp"] > 1
+    targs.recompute = cfg.recompute
+    targs.layers, targs.heads, targs.embd = cfg.layers, cfg.heads, cfg.embd
+    targs.block, targs.vocab = cfg.block, cfg.vocab
+    targs.batch = cfg.batch(lay)
+    targs.micro = cfg.micro
     targs.seed = 1337
     tr = Trainer(targs)
     dev = tr.device
-    batches = [tr.shard.get_batch(i, pin=True) for i in range(max(a.steps, a.warmup))]
+    n_batches = max(a.steps, a.warmup)
+    batches = [tr.shard.get_batch(i, pin=True) for i in range(n_batches)]
     dev_batches = [(x.to(dev), y.to(dev)) for x, y in batches]
     for i in range(a.warmup):
-        tr.step_device(*dev_batches[i % len(dev_batches)])
+        tr.step_device(*dev_batches[i % n_batches])
     torch.cuda.synchronize()
     sampler = ClockSampler() if rank == 0 else None
     losses = []
@@ -197,7 +278,7 @@ def run_ours(a, rank, world):
         losses.append(tr.step_device(*dev_batches[i]))
 
     ms = timed(dev_step, a.steps, sampler)
-    final_loss = float(losses[-1].float().item())
+    loss = final_loss(losses)
 
     def e2e_step(i):
         tr.step(*batches[i])
@@ -216,18 +297,19 @@ def run_ours(a, rank, world):
     return dict(
         ms=ms,
         e2e_ms=e2e_ms,
-        loss=final_loss,
+        loss=loss,
         launches=(ours, other, top_other),
         h2d=h2d,
-        d2h=4,
+        d2h=4 if tr.pp.is_last else 0,
         sampler=sampler,
         status=status,
         n_params=tr.n_params,
+        note=None,
     )
 
 
 # ---------------------------------------------------------------- reference arm
-def run_reference(a, rank, world):
+def run_reference(a, cfg: BenchConfig, lay: dict, rank, world):
     ref_root = os.path.join(HERE, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref_root, "dst")):
         return {"unavailable": "reference not installed under baseline/_ref"}
@@ -237,32 +319,52 @@ def run_reference(a, rank, world):
     from dst import parallel as rparallel  # the reference package
     from dst.data import SyntheticShard
     from dst.dp import GradReducer
-    from dst.model import GPT, GPTConfig
+    from dst.model import GPT, GPTConfig, GPTStage
+    from dst.pipeline import Pipeline1F1B
     from dst.precision import MasterWeightOptimizer
 
     assert os.path.abspath(rparallel.__file__).startswith(os.path.abspath(ref_root))
+    note = None
+    if lay["chunks"] > 1:
+        # The reference's interleaved schedule deadlocks on NCCL with tp > 1
+        # (its README.md:275-283: spinning p2p kernels across channel
+        # communicators), so it is not run; its 1F1B schedule on the same
+        # shape and layout is the comparison point.
+        note = "reference interleaved schedule not run (documented NCCL deadlock, README.md:275-283); 1F1B same shape"
     rparallel.init_distributed()
-    tp, pp, dp = rparallel.make_topology(1, 1, world)
+    tp, pp, dp = rparallel.make_topology(lay["tp"], lay["pp"], lay["dp"])
     dev = rparallel.default_device()
-    cfg = GPTConfig(
-        vocab_size=MODEL["vocab"],
-        block_size=MODEL["block"],
-        n_layer=MODEL["layers"],
-        n_head=MODEL["heads"],
-        n_embd=MODEL["embd"],
+    rcfg = GPTConfig(
+        vocab_size=cfg.vocab,
+        block_size=cfg.block,
+        n_layer=cfg.layers,
+        n_head=cfg.heads,
+        n_embd=cfg.embd,
         dropout=0.0,
+        sequence_parallel=cfg.sp and lay["tp"] > 1,
+        recompute_attention=cfg.recompute,
+        vocab_parallel_loss=cfg.vp and lay["tp"] > 1,
     )
-    model = GPT(cfg, tp, seed=1337).to(dev).to(torch.bfloat16)
+    # Model / schedule / optimizer / reducer as the reference's train.py:81-106.
+    model = GPTStage(rcfg, tp, pp, seed=1337) if lay["pp"] > 1 else GPT(rcfg, tp, seed=1337)
+    model = model.to(dev).to(torch.bfloat16)
+    pipe = Pipeline1F1B(model, pp, micro_batch_size=cfg.micro, seq_len=rcfg.block_size) if lay["pp"] > 1 else None
     opt = MasterWeightOptimizer(model.parameters(), lr=3e-4)
-    reducer = GradReducer(model, dp) if dp.enabled else None
-    shard = SyntheticShard(cfg.vocab_size, cfg.block_size, MICRO, seed=1337, dp=dp)
-    batches = [tuple(t.pin_memory() for t in shard.get_batch(i)) for i in range(max(a.steps, a.warmup))]
+    reducer = GradReducer(model, dp, overlap=(pipe is None)) if dp.enabled else None
+    shard = SyntheticShard(rcfg.vocab_size, rcfg.block_size, cfg.batch(lay), seed=1337, dp=dp)
+    n_batches = max(a.steps, a.warmup)
+    batches = [tuple(t.pin_memory() for t in shard.get_batch(i)) for i in range(n_batches)]
     dev_batches = [(x.to(dev), y.to(dev)) for x, y in batches]
 
     def step_device(idx, tgt):
         opt.zero_grad(set_to_none=True)
-        _, loss = model(idx, tgt)
-        loss.backward()
+        if pipe is not None:
+            loss = pipe.train_step(idx, tgt)
+            if reducer is not None:
+                reducer.reduce()
+        else:
+            _, loss = model(idx, tgt)
+            loss.backward()
         if reducer is not None:
             reducer.finish()
         model.finalize_grads()
@@ -270,35 +372,38 @@ def run_reference(a, rank, world):
         return loss
 
     for i in range(a.warmup):
-        step_device(*dev_batches[i % len(dev_batches)])
+        step_device(*dev_batches[i % n_batches])
     torch.cuda.synchronize()
     sampler = ClockSampler() if rank == 0 else None
     losses = []
     ms = timed(lambda i: losses.append(step_device(*dev_batches[i])), a.steps, sampler)
-    final_loss = float(losses[-1].float().item())
+    loss = final_loss(losses)
 
     def e2e_step(i):
         x, y = batches[i]
-        loss = step_device(x.to(dev, non_blocking=True), y.to(dev, non_blocking=True))
-        loss.float().item()
+        out = step_device(x.to(dev, non_blocking=True), y.to(dev, non_blocking=True))
+        if out is not None:
+            out.float().item()
 
     e2e_ms = timed(e2e_step, a.steps) if not a.no_e2e else float("nan")
     x0, y0 = batches[0]
     return dict(
         ms=ms,
         e2e_ms=e2e_ms,
-        loss=final_loss,
+        loss=loss,
         launches=None,
         h2d=x0.numel() * x0.element_size() + y0.numel() * y0.element_size(),
-        d2h=4,
+        d2h=4 if pp.is_last else 0,
         sampler=sampler,
         status=None,
         n_params=sum(p.numel() for p in model.parameters()),
+        note=note,
     )
 
 
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c2")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
@@ -311,15 +416,23 @@ def main():
     rank, world = setup_env()
     if world != a.gpus:
         raise SystemExit(f"--gpus {a.gpus} but world size {world}")
-    res = run_reference(a, rank, world) if a.impl == "reference" else run_ours(a, rank, world)
+    cfg = CONFIGS[a.config]
+    lay = cfg.layout(world)
+    if lay is None:
+        if rank == 0:
+            print(json.dumps({"impl": a.impl, "config": a.config, "n_gpus": world,
+                              "unavailable": f"config {a.config} has no layout for {world} GPU(s)"}), flush=True)
+        return
+    res = run_reference(a, cfg, lay, rank, world) if a.impl == "reference" else run_ours(a, cfg, lay, rank, world)
     if "unavailable" in res:
         if rank == 0:
             print(json.dumps({"impl": "reference", "unavailable": res["unavailable"]}), flush=True)
         return
-    tokens = MICRO * MODEL["block"] * world
+    batch = cfg.batch(lay)
+    tokens = batch * cfg.block * lay["dp"]
     value = tokens / (res["ms"] / 1000.0)
     e2e = tokens / (res["e2e_ms"] / 1000.0)
-    pub = PUBLISHED.get(world)
+    pub = (cfg.published or {}).get(world)
     out = {
         "metric": "tokens/sec (whole box, device-timed, max over ranks)",
         "value": round(value, 1),
@@ -329,20 +442,23 @@ def main():
         "warmup": a.warmup,
         "ms_per_step": round(res["ms"], 3),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": cfg.scaling,
         "vs_baseline": round(value / pub, 3) if pub else None,
         "dtype": "bf16",
         "data": "synthetic (uniform random token ids, seeded; random-init weights)",
         "config": {
-            "model": "GPT-2 small 12L/768/12H, d_ff 3072, seq 1024, vocab 50304 (BASELINE config 2)",
-            "global_batch": MICRO * world,
-            "micro_batch_per_rank": MICRO,
-            "seq_len": MODEL["block"],
-            "parallelism": f"dp{world}",
-            "optimizer": "Adam on fp32 masters, bf16 params (MasterWeightOptimizer)",
+            "name": cfg.name,
+            "model": cfg.description,
+            "global_batch": batch * lay["dp"],
+            "micro_batch": cfg.micro,
+            "seq_len": cfg.block,
+            "parallelism": f"dp{world}" if cfg.name == "c2" else parallelism_name(lay),
+            "sequence_parallel": cfg.sp and lay["tp"] > 1,
+            "recompute": cfg.recompute,
+            "optimizer": "Adam on fp32 masters, bf16 params",
             "dp_buckets_mb": 25,
             "l2": "no flush: each step streams several GB of weights/optimizer state/activations (>> 126 MB L2)",
-            "params": res["n_params"],
+            "params_rank0": res["n_params"],
             "final_loss": round(res["loss"], 4),
         },
         "e2e": {
@@ -353,6 +469,8 @@ def main():
             "ms_per_step": round(res["e2e_ms"], 3),
         },
     }
+    if res.get("note"):
+        out["note"] = res["note"]
     if res["sampler"] is not None:
         out["clocks"] = res["sampler"].summary()
     if a.impl == "reference":

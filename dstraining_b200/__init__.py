@@ -9,4 +9,14 @@ Adam, fused DP reduce + Adam), ``utils`` (data, checkpoints, timing). The
 API on top of these.
 """
 
+import os
+
+# Load every kernel when the CUDA context is created instead of at its first
+# launch. With lazy loading, the first launch of a kernel waits for the device
+# to go idle; a pipeline stage that has posted an NCCL receive ahead of time
+# (a kernel spinning until the peer sends), or a fused collective spinning on
+# a peer's flag, never goes idle while that peer is stuck in the same way, so
+# both ranks would wait forever. Must be set before the context exists.
+os.environ.setdefault("CUDA_MODULE_LOADING", "EAGER")
+
 __version__ = "0.1.0"

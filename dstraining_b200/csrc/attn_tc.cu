@@ -335,29 +335,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 
-// ------------------------------------------------------------------ backward
-// Di[b, h, t] = sum_d dO[b, t, h, d] * O[b, t, h, d]; one warp per (b, t, h).
-__global__ void bwd_rowdot_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ out,
-                                  float* __restrict__ di, int rows, int T, int H, int D) {
-  const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (w >= rows) return;
-  const __nv_bfloat16* a = dout + static_cast<size_t>(w) * D;
-  const __nv_bfloat16* c = out + static_cast<size_t>(w) * D;
-  float acc = 0.f;
-  for (int d = lane * 2; d < D; d += 64) {
-    const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(a + d));
-    const float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(c + d));
-    acc += x.x * y.x + x.y * y.y;
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffff, acc, o);
-  if (lane == 0) {
-    const int hh = w % H, bt = w / H;
-    di[(static_cast<size_t>(bt / T) * H + hh) * T + bt % T] = acc;
-  }
-}
-
 __device__ __forceinline__ void store_row_bf16(__nv_bfloat16* dst, const float (&v)[32], float scale) {
 #pragma unroll
   for (int i = 0; i < 32; i += 8) {
@@ -371,6 +348,302 @@ __device__ __forceinline__ void store_row_bf16(__nv_bfloat16* dst, const float (
     *reinterpret_cast<uint4*>(dst + i) = pk;
   }
 }
+
+// ------------------------------------------------------- ping-pong forward
+// Two 128-query tiles per CTA (256 queries of one (batch, head)), 10 warps:
+//   warp 0     TMA: Q0 and Q1 once, then K_0, V_0, K_1, V_1, ... through one
+//              ring of kSlots tiles (released strictly in load order).
+//   warp 1     MMA issuer. Steady-state order
+//                PV0_j, S0_{j+1}, PV1_j, S1_{j+1}
+//              so the tensor core works on one tile while the other tile's
+//              softmax runs; S_g,j and O_g live in TMEM (columns S0 0-127,
+//              S1 128-255, O0 256.., O1 256+D..), O accumulating across key
+//              blocks.
+//   warps 2-5  softmax of tile 0, warps 6-9 softmax of tile 1: one thread per
+//              query row, all 128 key columns of S (no cross-warp exchange).
+// Rescaling of O is conditional: a row keeps its reference maximum until a
+// block's maximum exceeds it by more than 8 (log2 units), so probabilities
+// stay below 2^8 and the TMEM read-modify-write of the row's O is rare
+// after the first blocks. A commit on S_g,{j+1} also covers PV_g,j, so a
+// softmax thread that holds S_g,j may rewrite its O row and the P_g tile
+// without further waits. The last key block of tile 1 has no tile-0 work
+// (tile 0 ends one block earlier on the causal diagonal).
+template <int D>
+struct PPCfg {
+  static constexpr int kDAtoms = D / 64;
+  static constexpr int kTile = kDAtoms * kAtom;      // 128 rows x D
+  static constexpr int kSlots = (D == 64) ? 4 : 3;   // K/V ring
+  static constexpr int kPTile = 2 * kAtom;           // 128 rows x 128 keys
+  static constexpr int kBars = 1 + 2 * 4 + 2 + 2 + 2 + 1;
+  static constexpr int kSmem = 2 * kTile + kSlots * kTile + 2 * kPTile + kBars * 8 + 16 + 1024;
+  static_assert(kSmem <= 232448, "ping-pong forward: shared memory");
+};
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    fwd_pp_kernel(const __grid_constant__ CUtensorMap tmQKV, __nv_bfloat16* __restrict__ out,
+                  float* __restrict__ lse2, int T, int H, float scale_log2, int* status) {
+  using C = PPCfg<D>;
+  constexpr int S = C::kSlots;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                       // [2][kTile]
+  uint8_t* sRing = sQ + 2 * C::kTile;       // [S][kTile]
+  uint8_t* sP = sRing + S * C::kTile;       // [2][kPTile]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * C::kPTile);
+  uint64_t* q_full = bars;
+  uint64_t* ring_full = bars + 1;           // [S] (S <= 4)
+  uint64_t* ring_empty = bars + 5;          // [S]
+  uint64_t* s_full = bars + 9;              // [2]
+  uint64_t* p_full = bars + 11;             // [2]
+  uint64_t* o_final = bars + 13;            // [2]
+  uint64_t* drained = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kBars);
+
+  const int cb = gridDim.x - 1 - blockIdx.x;  // heaviest blocks first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nkb0 = 2 * cb + 1, nkb1 = 2 * cb + 2;  // key blocks of tile 0 / tile 1
+  const int row0 = b * T;
+  const int q0 = cb * 256;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&ring_full[i], 1);
+      mbar_init(&ring_empty[i], 1);
+    }
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(&s_full[g], 1);
+      mbar_init(&p_full[g], 128);
+      mbar_init(&o_final[g], 1);
+    }
+    mbar_init(drained, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      tma_prefetch_desc(&tmQKV);
+      mbar_arrive_expect_tx(q_full, 2 * C::kTile);
+#pragma unroll
+      for (int g = 0; g < 2; ++g)
+#pragma unroll
+        for (int a = 0; a < C::kDAtoms; ++a)
+          tma_load_2d(sQ + g * C::kTile + a * kAtom, &tmQKV, q_full, h * 3 * D + a * 64, row0 + q0 + g * 128);
+      int last = -1;
+      for (int t = 0; t < 2 * nkb1; ++t) {
+        const int slot = t % S, n = t / S;
+        if (!mbar_wait(&ring_empty[slot], (n & 1) ^ 1, status, kTimeoutSmemEmpty)) break;
+        mbar_arrive_expect_tx(&ring_full[slot], C::kTile);
+        const int col = h * 3 * D + ((t & 1) ? 2 * D : D);
+#pragma unroll
+        for (int a = 0; a < C::kDAtoms; ++a)
+          tma_load_2d(sRing + slot * C::kTile + a * kAtom, &tmQKV, &ring_full[slot], col + a * 64,
+                      row0 + (t >> 1) * 128);
+        last = t;
+      }
+      // no copy may still be landing when the CTA exits
+      mbar_wait(q_full, 0, status, kTimeoutTmaFull);
+      if (last >= 0) mbar_wait(&ring_full[last % S], (last / S) & 1, status, kTimeoutTmaFull);
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idS = idesc_bf16_f32(128, 128, false, false);
+      constexpr uint32_t idPV = idesc_bf16_f32(128, D, false, true);
+      auto wait_tile = [&](int t) -> bool {
+        return mbar_wait(&ring_full[t % S], (t / S) & 1, status, kTimeoutTmaFull);
+      };
+      auto issue_s = [&](int g, int t) {  // S_g = Q_g K^T, K in ring tile t
+        const uint32_t q_addr = smem_u32(sQ + g * C::kTile), k_addr = smem_u32(sRing + (t % S) * C::kTile);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kAtom + (kk & 3) * 32;
+          umma_f16_ss(tmem + g * 128, smem_desc_sw128(q_addr + off, 16, 1024),
+                      smem_desc_sw128(k_addr + off, 16, 1024), idS, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[g]);
+      };
+      auto issue_pv = [&](int g, int t, bool acc) {  // O_g (+)= P_g V, V in ring tile t
+        const uint32_t p_addr = smem_u32(sP + g * C::kPTile), v_addr = smem_u32(sRing + (t % S) * C::kTile);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t poff = (kk >> 2) * kAtom + (kk & 3) * 32;
+          umma_f16_ss(tmem + 256 + g * D, smem_desc_sw128(p_addr + poff, 16, 1024),
+                      smem_desc_sw128(v_addr + kk * 2048, kAtom, 1024), idPV, (acc || kk > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(q_full, 0, status, kTimeoutTmaFull) && wait_tile(0);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
+        umma_commit(&ring_empty[0]);  // K_0 consumed by both tiles
+      }
+      for (int j = 0; j < nkb1 && ok; ++j) {
+        const int tv = 2 * j + 1, tk = 2 * j + 2;  // V_j, K_{j+1}
+        bool k_ready = false;
+        ok = wait_tile(tv);
+        if (ok && j < nkb0) {
+          ok = mbar_wait(&p_full[0], j & 1, status, kTimeoutTmemFull);
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv(0, tv, j > 0);
+          if (j == nkb0 - 1) umma_commit(&o_final[0]);
+          if (j + 1 < nkb0) {
+            ok = wait_tile(tk);
+            if (!ok) break;
+            k_ready = true;
+            issue_s(0, tk);
+          }
+        }
+        if (!ok) break;
+        ok = mbar_wait(&p_full[1], j & 1, status, kTimeoutTmemFull);
+        if (!ok) break;
+        tc_fence_after();
+        issue_pv(1, tv, j > 0);
+        umma_commit(&ring_empty[tv % S]);  // V_j consumed by both tiles
+        if (j == nkb1 - 1) umma_commit(&o_final[1]);
+        if (j + 1 < nkb1) {
+          if (!k_ready) ok = wait_tile(tk);
+          if (!ok) break;
+          issue_s(1, tk);
+          umma_commit(&ring_empty[tk % S]);  // K_{j+1} consumed by both tiles
+        }
+      }
+      umma_commit(drained);  // every MMA issued above has completed
+      mbar_wait(drained, 0, status, kTimeoutTmemFull);
+    }
+    __syncwarp();
+  } else {
+    const int grp = (warp - 2) >> 2;  // the query tile of this warp
+    const int quad = warp & 3;        // TMEM lane quadrant this warp may access
+    const int r = quad * 32 + lane;
+    const int q = q0 + grp * 128 + r;
+    const int nkb = nkb0 + grp;
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    const uint32_t tS = tmem + grp * 128 + lane_off;
+    const uint32_t tO = tmem + 256 + grp * D + lane_off;
+    uint8_t* pbuf = sP + grp * C::kPTile;
+    float m_ref = -INFINITY, l = 0.f;
+    bool alive = true;
+    for (int j = 0; j < nkb; ++j) {
+      // tcgen05.ld / st are warp-collective (.sync.aligned): every branch
+      // around them is decided by the whole warp
+      if (!__all_sync(0xffffffff, mbar_wait(&s_full[grp], j & 1, status, kTimeoutTmemFull))) {
+        alive = false;
+        break;
+      }
+      tc_fence_after();
+      const bool diag = (j == nkb - 1);
+      const int kbase = j * 128;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        float v[64];
+        tmem_ld64_sync(tS + hh * 64, v);
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          const bool masked = diag && (kbase + hh * 64 + i > q);
+          mx = fmaxf(mx, masked ? -INFINITY : v[i]);
+        }
+      }
+      const float m_blk = mx * scale_log2;
+      const bool need = m_blk > m_ref + 8.f;  // this row's reference maximum moves
+      const float c = need ? exp2f(m_ref - m_blk) : 1.f;
+      if (need) {
+        l *= c;
+        m_ref = m_blk;
+      }
+      if (j > 0 && __any_sync(0xffffffff, need)) {  // whole warp; other rows scale by 1
+#pragma unroll 1
+        for (int ch = 0; ch < D / 32; ++ch) {
+          float o[32];
+          tmem_ld32_sync(tO + ch * 32, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= c;
+          tmem_st32_sync(tO + ch * 32, o);
+        }
+      }
+      float rowsum = 0.f;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        float v[64];
+        tmem_ld64_sync(tS + hh * 64, v);
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          const bool masked = diag && (kbase + hh * 64 + i > q);
+          v[i] = masked ? 0.f : exp2f(v[i] * scale_log2 - m_ref);
+          rowsum += v[i];
+        }
+        store_p_quarter(pbuf, r, hh * 2, *reinterpret_cast<const float(*)[32]>(v));
+        store_p_quarter(pbuf, r, hh * 2 + 1, *reinterpret_cast<const float(*)[32]>(v + 32));
+      }
+      l += rowsum;
+      tc_fence_before();
+      fence_proxy_async_smem();
+      mbar_arrive(&p_full[grp]);
+    }
+    if (__all_sync(0xffffffff, alive && mbar_wait(&o_final[grp], 0, status, kTimeoutTmemFull))) {
+      tc_fence_after();
+      const float inv = 1.f / l;
+      __nv_bfloat16* orow = out + (static_cast<size_t>(row0 + q) * H + h) * D;
+#pragma unroll
+      for (int ch = 0; ch < D / 32; ++ch) {
+        float o[32];
+        tmem_ld32_sync(tO + ch * 32, o);
+        store_row_bf16(orow + ch * 32, o, inv);
+      }
+      lse2[(static_cast<size_t>(b) * H + h) * T + q] = m_ref + log2f(l);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------ backward
+// Di[b, h, t] = sum_d dO[b, t, h, d] * O[b, t, h, d]. D/8 threads per
+// (b, t, h) row, one 16-byte load of each operand per thread, so a warp reads
+// 32 * 16 contiguous bytes of each tensor; the partial sums meet by shuffles.
+template <int D>
+__global__ void bwd_rowdot_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ out,
+                                  float* __restrict__ di, int rows, int T, int H) {
+  constexpr int kPer = D / 8;  // threads per row
+  const int64_t gt = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t w = gt / kPer;
+  const int part = static_cast<int>(gt % kPer);
+  float acc = 0.f;
+  if (w < rows) {
+    const uint4 a = *reinterpret_cast<const uint4*>(dout + w * D + part * 8);
+    const uint4 c = *reinterpret_cast<const uint4*>(out + w * D + part * 8);
+    const __nv_bfloat162* ah = reinterpret_cast<const __nv_bfloat162*>(&a);
+    const __nv_bfloat162* ch = reinterpret_cast<const __nv_bfloat162*>(&c);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 x = __bfloat1622float2(ah[j]), y = __bfloat1622float2(ch[j]);
+      acc += x.x * y.x + x.y * y.y;
+    }
+  }
+#pragma unroll
+  for (int o = kPer / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffff, acc, o);
+  if (w < rows && part == 0) {
+    const int64_t hh = w % H, bt = w / H;
+    di[(bt / T * H + hh) * T + bt % T] = acc;
+  }
+}
+
 
 // dK / dV: one CTA per (128-key block, head, batch), walking the query blocks
 // (BQ rows) at or after the key block. Per query block:
@@ -547,7 +820,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async_smem();
       mbar_arrive(p_full);
     }
-    if (ok && mbar_wait(fin, 0, status, kTimeoutTmemFull)) {
+    if (__all_sync(0xffffffff, ok && mbar_wait(fin, 0, status, kTimeoutTmemFull))) {
       tc_fence_after();
       __nv_bfloat16* krow = dqkv + (static_cast<size_t>(row0 + key) * H + h) * 3 * D + D + half * (D / 2);
       __nv_bfloat16* vrow = krow + D;
@@ -730,7 +1003,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async_smem();
       mbar_arrive(p_full);
     }
-    if (ok && mbar_wait(fin, 0, status, kTimeoutTmemFull)) {
+    if (__all_sync(0xffffffff, ok && mbar_wait(fin, 0, status, kTimeoutTmemFull))) {
       tc_fence_after();
       __nv_bfloat16* qrow = dqkv + (static_cast<size_t>(row0 + q) * H + h) * 3 * D + half * (D / 2);
 #pragma unroll
@@ -750,13 +1023,429 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ------------------------------------------------ double-buffered backward
+// The same two deterministic kernels as above, restructured so that the
+// tensor core and the softmax warps overlap: S and dP of block i+1 are
+// computed into the second pair of TMEM buffers while the softmax warps turn
+// block i into P and dS, and the dV/dK (or dQ) MMAs of block i run one step
+// later. Blocks are 64 wide (BQ / BK = 64) so that two S/dP pairs plus the
+// accumulators fit in TMEM (4 x 64 + 2 x D <= 512 columns); operands stream
+// through a 3-stage ring so a TMA load has a full iteration of slack.
+//
+// dK/dV, one CTA per (128-key block, head, batch), per 64-query block i:
+//   MMA:     S^T_i = K Q_i^T, dP^T_i = V dO_i^T -> TMEM pair i % 2
+//            then dV += P^T_{i-1} dO_{i-1}, dK += dS^T_{i-1} Q_{i-1}
+//   softmax: P^T = exp2(S^T * scale - lse2[q]) (0 above the diagonal),
+//            dS^T = P^T * (dP^T - Di[q]) -> shared tiles i % 2
+template <int D>
+struct DkdvDbCfg {
+  static constexpr int kDAtoms = D / 64;
+  static constexpr int kNS = 3;                    // Q / dO / lse / Di stages
+  static constexpr int kKVTile = kDAtoms * kAtom;  // 128 keys x D
+  static constexpr int kQAtom = 64 * 128;          // 64 rows x 64 columns
+  static constexpr int kQTile = kDAtoms * kQAtom;  // 64 queries x D
+  static constexpr int kPTile = kAtom;             // 128 keys x 64 queries
+  static constexpr int kBars = 1 + 2 * kNS + 2 * 4 + 1;
+  static constexpr int kSmem = 2 * kKVTile + 2 * kNS * kQTile + 4 * kPTile + 2 * kNS * 64 * 4 + kBars * 8 + 16 + 1024;
+  static_assert(kSmem <= 232448, "dK/dV: shared memory");
+};
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    dkdv_db_kernel(const __grid_constant__ CUtensorMap tmKV, const __grid_constant__ CUtensorMap tmQ,
+                   const __grid_constant__ CUtensorMap tmDO, const float* __restrict__ lse2,
+                   const float* __restrict__ di, __nv_bfloat16* __restrict__ dqkv, int T, int H, float scale_log2,
+                   float scale, int* status) {
+  using C = DkdvDbCfg<D>;
+  constexpr int NS = C::kNS;
+  constexpr int BQ = 64;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + C::kKVTile;
+  uint8_t* sQ = sV + C::kKVTile;          // [NS][kQTile]
+  uint8_t* sDO = sQ + NS * C::kQTile;     // [NS][kQTile]
+  uint8_t* sP = sDO + NS * C::kQTile;     // [2][kPTile]
+  uint8_t* sDS = sP + 2 * C::kPTile;      // [2][kPTile]
+  float* sL = reinterpret_cast<float*>(sDS + 2 * C::kPTile);  // [NS][64]
+  float* sDi = sL + NS * BQ;                                  // [NS][64]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDi + NS * BQ);
+  uint64_t* kv_full = bars;
+  uint64_t* q_full = bars + 1;          // [NS]
+  uint64_t* q_empty = q_full + NS;      // [NS]
+  uint64_t* s_full = q_empty + NS;      // [2]
+  uint64_t* s_free = s_full + 2;        // [2]
+  uint64_t* p_full = s_free + 2;        // [2]
+  uint64_t* pds_free = p_full + 2;      // [2]
+  uint64_t* fin = pds_free + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kBars);
+
+  const int kb = blockIdx.x;  // key block 0 has the most query blocks: first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = b * T, k0 = kb * BM;
+  const int qb0 = k0 / BQ;
+  const int nq = T / BQ - qb0;
+  const float* lrow = lse2 + (static_cast<size_t>(b) * H + h) * T;
+  const float* drow = di + (static_cast<size_t>(b) * H + h) * T;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 256);
+      mbar_init(&p_full[i], 256);
+      mbar_init(&pds_free[i], 1);
+    }
+    mbar_init(fin, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tDP = tmem + 128, tDV = tmem + 256, tDK = tmem + 256 + D;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      mbar_arrive_expect_tx(kv_full, 2 * C::kKVTile);
+#pragma unroll
+      for (int a = 0; a < C::kDAtoms; ++a) {
+        tma_load_2d(sK + a * kAtom, &tmKV, kv_full, h * 3 * D + D + a * 64, row0 + k0);
+        tma_load_2d(sV + a * kAtom, &tmKV, kv_full, h * 3 * D + 2 * D + a * 64, row0 + k0);
+      }
+      int last = -1;
+      for (int i = 0; i < nq; ++i) {
+        const int st = i % NS;
+        if (!mbar_wait(&q_empty[st], ((i / NS) & 1) ^ 1, status, kTimeoutSmemEmpty)) break;
+        const int q0 = (qb0 + i) * BQ;
+        mbar_arrive_expect_tx(&q_full[st], 2 * C::kQTile + 2 * BQ * 4);
+#pragma unroll
+        for (int a = 0; a < C::kDAtoms; ++a) {
+          tma_load_2d(sQ + st * C::kQTile + a * C::kQAtom, &tmQ, &q_full[st], h * 3 * D + a * 64, row0 + q0);
+          tma_load_2d(sDO + st * C::kQTile + a * C::kQAtom, &tmDO, &q_full[st], h * D + a * 64, row0 + q0);
+        }
+        bulk_load(sL + st * BQ, lrow + q0, BQ * 4, &q_full[st]);
+        bulk_load(sDi + st * BQ, drow + q0, BQ * 4, &q_full[st]);
+        last = i;
+      }
+      mbar_wait(kv_full, 0, status, kTimeoutTmaFull);
+      if (last >= 0) mbar_wait(&q_full[last % NS], (last / NS) & 1, status, kTimeoutTmaFull);
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idS = idesc_bf16_f32(BM, BQ, false, false);
+      constexpr uint32_t idG = idesc_bf16_f32(BM, D, false, true);
+      bool ok = mbar_wait(kv_full, 0, status, kTimeoutTmaFull);
+      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+      for (int i = 0; i <= nq && ok; ++i) {
+        if (i < nq) {
+          const int st = i % NS, pb = i & 1;
+          ok = mbar_wait(&q_full[st], (i / NS) & 1, status, kTimeoutTmaFull) &&
+               mbar_wait(&s_free[pb], ((i >> 1) & 1) ^ 1, status, kTimeoutTmemEmpty);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t q_addr = smem_u32(sQ + st * C::kQTile), do_addr = smem_u32(sDO + st * C::kQTile);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t a_off = (kk >> 2) * kAtom + (kk & 3) * 32;
+            const uint32_t b_off = (kk >> 2) * C::kQAtom + (kk & 3) * 32;
+            umma_f16_ss(tS + pb * 64, smem_desc_sw128(k_addr + a_off, 16, 1024),
+                        smem_desc_sw128(q_addr + b_off, 16, 1024), idS, kk > 0 ? 1u : 0u);
+            umma_f16_ss(tDP + pb * 64, smem_desc_sw128(v_addr + a_off, 16, 1024),
+                        smem_desc_sw128(do_addr + b_off, 16, 1024), idS, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[pb]);
+        }
+        if (i >= 1) {
+          const int j = i - 1, sj = j % NS, pb = j & 1;
+          ok = mbar_wait(&p_full[pb], (j >> 1) & 1, status, kTimeoutTmaFull);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t q_addr = smem_u32(sQ + sj * C::kQTile), do_addr = smem_u32(sDO + sj * C::kQTile);
+          const uint32_t p_addr = smem_u32(sP + pb * C::kPTile), ds_addr = smem_u32(sDS + pb * C::kPTile);
+#pragma unroll
+          for (int kk = 0; kk < BQ / 16; ++kk) {
+            const uint32_t a_off = (kk & 3) * 32;
+            const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
+            umma_f16_ss(tDV, smem_desc_sw128(p_addr + a_off, 16, 1024),
+                        smem_desc_sw128(do_addr + kk * 2048, C::kQAtom, 1024), idG, acc);
+            umma_f16_ss(tDK, smem_desc_sw128(ds_addr + a_off, 16, 1024),
+                        smem_desc_sw128(q_addr + kk * 2048, C::kQAtom, 1024), idG, acc);
+          }
+          umma_commit(&q_empty[sj]);
+          umma_commit(&pds_free[pb]);
+        }
+      }
+      umma_commit(fin);
+      mbar_wait(fin, 0, status, kTimeoutTmemFull);
+    }
+    __syncwarp();
+  } else {
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;  // query columns [32 half, 32 half + 32)
+    const int r = quad * 32 + lane;
+    const int key = k0 + r;
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    const int col = half * 32;
+    bool ok = true;
+    for (int i = 0; i < nq && ok; ++i) {
+      const int st = i % NS, pb = i & 1;
+      const uint32_t ph = (i >> 1) & 1;
+      ok = __all_sync(0xffffffff, mbar_wait(&q_full[st], (i / NS) & 1, status, kTimeoutTmaFull) &&
+                                      mbar_wait(&s_full[pb], ph, status, kTimeoutTmemFull) &&
+                                      mbar_wait(&pds_free[pb], ph ^ 1, status, kTimeoutTmemFull));
+      if (!ok) break;
+      tc_fence_after();
+      float sv[32], dp[32];
+      tmem_ld32x2_sync(tS + pb * 64 + col + lane_off, tDP + pb * 64 + col + lane_off, sv, dp);
+      tc_fence_before();
+      mbar_arrive(&s_free[pb]);  // the TMEM pair may take block i + 2
+      const int q0 = (qb0 + i) * BQ;
+      const float* lq = sL + st * BQ + col;
+      const float* dq = sDi + st * BQ + col;
+#pragma unroll
+      for (int t = 0; t < 32; ++t) {
+        const float p = (key > q0 + col + t) ? 0.f : exp2f(sv[t] * scale_log2 - lq[t]);
+        sv[t] = p;
+        dp[t] = p * (dp[t] - dq[t]);
+      }
+      store_p_quarter(sP + pb * C::kPTile, r, half, sv);
+      store_p_quarter(sDS + pb * C::kPTile, r, half, dp);
+      fence_proxy_async_smem();
+      mbar_arrive(&p_full[pb]);
+    }
+    if (__all_sync(0xffffffff, ok && mbar_wait(fin, 0, status, kTimeoutTmemFull))) {
+      tc_fence_after();
+      __nv_bfloat16* krow = dqkv + (static_cast<size_t>(row0 + key) * H + h) * 3 * D + D + half * (D / 2);
+      __nv_bfloat16* vrow = krow + D;
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        float v[32];
+        tmem_ld32_sync(tDK + half * (D / 2) + c * 32 + lane_off, v);
+        store_row_bf16(krow + c * 32, v, scale);
+        tmem_ld32_sync(tDV + half * (D / 2) + c * 32 + lane_off, v);
+        store_row_bf16(vrow + c * 32, v, 1.f);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// dQ, one CTA per (128-query block, head, batch), per 64-key block j up to the
+// diagonal:
+//   MMA:     S_j = Q K_j^T, dP_j = dO V_j^T -> TMEM pair j % 2
+//            then dQ += dS_{j-1} K_{j-1}
+//   softmax: dS = exp2(S * scale - lse2) * (dP - Di) -> shared tile j % 2
+template <int D>
+struct DqDbCfg {
+  static constexpr int kDAtoms = D / 64;
+  static constexpr int kNS = 3;                    // K / V stages
+  static constexpr int kQTile = kDAtoms * kAtom;   // 128 queries x D
+  static constexpr int kKAtom = 64 * 128;
+  static constexpr int kKTile = kDAtoms * kKAtom;  // 64 keys x D
+  static constexpr int kSTile = kAtom;             // 128 queries x 64 keys
+  static constexpr int kBars = 1 + 2 * kNS + 2 * 4 + 1;
+  static constexpr int kSmem = 2 * kQTile + 2 * kNS * kKTile + 2 * kSTile + kBars * 8 + 16 + 1024;
+  static_assert(kSmem <= 232448, "dQ: shared memory");
+};
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    dq_db_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
+                 const __grid_constant__ CUtensorMap tmKV, const float* __restrict__ lse2, const float* __restrict__ di,
+                 __nv_bfloat16* __restrict__ dqkv, int T, int H, float scale_log2, float scale, int* status) {
+  using C = DqDbCfg<D>;
+  constexpr int NS = C::kNS;
+  constexpr int BK = 64;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sDO = sQ + C::kQTile;
+  uint8_t* sK = sDO + C::kQTile;       // [NS][kKTile]
+  uint8_t* sV = sK + NS * C::kKTile;   // [NS][kKTile]
+  uint8_t* sDS = sV + NS * C::kKTile;  // [2][kSTile]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDS + 2 * C::kSTile);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;         // [NS]
+  uint64_t* kv_empty = kv_full + NS;    // [NS]
+  uint64_t* s_full = kv_empty + NS;     // [2]
+  uint64_t* s_free = s_full + 2;        // [2]
+  uint64_t* p_full = s_free + 2;        // [2]
+  uint64_t* ds_free = p_full + 2;       // [2]
+  uint64_t* fin = ds_free + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kBars);
+
+  const int qb = gridDim.x - 1 - blockIdx.x;  // heaviest (most key blocks) first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = b * T, q0 = qb * BM;
+  const int nkb = (q0 + BM - 1) / BK + 1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 256);
+      mbar_init(&p_full[i], 256);
+      mbar_init(&ds_free[i], 1);
+    }
+    mbar_init(fin, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tDP = tmem + 128, tDQ = tmem + 256;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      mbar_arrive_expect_tx(q_full, 2 * C::kQTile);
+#pragma unroll
+      for (int a = 0; a < C::kDAtoms; ++a) {
+        tma_load_2d(sQ + a * kAtom, &tmQ, q_full, h * 3 * D + a * 64, row0 + q0);
+        tma_load_2d(sDO + a * kAtom, &tmDO, q_full, h * D + a * 64, row0 + q0);
+      }
+      int last = -1;
+      for (int j = 0; j < nkb; ++j) {
+        const int st = j % NS;
+        if (!mbar_wait(&kv_empty[st], ((j / NS) & 1) ^ 1, status, kTimeoutSmemEmpty)) break;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * C::kKTile);
+#pragma unroll
+        for (int a = 0; a < C::kDAtoms; ++a) {
+          tma_load_2d(sK + st * C::kKTile + a * C::kKAtom, &tmKV, &kv_full[st], h * 3 * D + D + a * 64, row0 + j * BK);
+          tma_load_2d(sV + st * C::kKTile + a * C::kKAtom, &tmKV, &kv_full[st], h * 3 * D + 2 * D + a * 64,
+                      row0 + j * BK);
+        }
+        last = j;
+      }
+      mbar_wait(q_full, 0, status, kTimeoutTmaFull);
+      if (last >= 0) mbar_wait(&kv_full[last % NS], (last / NS) & 1, status, kTimeoutTmaFull);
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idS = idesc_bf16_f32(BM, BK, false, false);
+      constexpr uint32_t idG = idesc_bf16_f32(BM, D, false, true);
+      bool ok = mbar_wait(q_full, 0, status, kTimeoutTmaFull);
+      const uint32_t q_addr = smem_u32(sQ), do_addr = smem_u32(sDO);
+      for (int j = 0; j <= nkb && ok; ++j) {
+        if (j < nkb) {
+          const int st = j % NS, pb = j & 1;
+          ok = mbar_wait(&kv_full[st], (j / NS) & 1, status, kTimeoutTmaFull) &&
+               mbar_wait(&s_free[pb], ((j >> 1) & 1) ^ 1, status, kTimeoutTmemEmpty);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t k_addr = smem_u32(sK + st * C::kKTile), v_addr = smem_u32(sV + st * C::kKTile);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t a_off = (kk >> 2) * kAtom + (kk & 3) * 32;
+            const uint32_t b_off = (kk >> 2) * C::kKAtom + (kk & 3) * 32;
+            umma_f16_ss(tS + pb * 64, smem_desc_sw128(q_addr + a_off, 16, 1024),
+                        smem_desc_sw128(k_addr + b_off, 16, 1024), idS, kk > 0 ? 1u : 0u);
+            umma_f16_ss(tDP + pb * 64, smem_desc_sw128(do_addr + a_off, 16, 1024),
+                        smem_desc_sw128(v_addr + b_off, 16, 1024), idS, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[pb]);
+        }
+        if (j >= 1) {
+          const int jj = j - 1, sj = jj % NS, pb = jj & 1;
+          ok = mbar_wait(&p_full[pb], (jj >> 1) & 1, status, kTimeoutTmaFull);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t k_addr = smem_u32(sK + sj * C::kKTile), ds_addr = smem_u32(sDS + pb * C::kSTile);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            umma_f16_ss(tDQ, smem_desc_sw128(ds_addr + (kk & 3) * 32, 16, 1024),
+                        smem_desc_sw128(k_addr + kk * 2048, C::kKAtom, 1024), idG, (jj > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&kv_empty[sj]);
+          umma_commit(&ds_free[pb]);
+        }
+      }
+      umma_commit(fin);
+      mbar_wait(fin, 0, status, kTimeoutTmemFull);
+    }
+    __syncwarp();
+  } else {
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;  // key columns [32 half, 32 half + 32)
+    const int r = quad * 32 + lane;
+    const int q = q0 + r;
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    const float lq = lse2[(static_cast<size_t>(b) * H + h) * T + q];
+    const float dq_i = di[(static_cast<size_t>(b) * H + h) * T + q];
+    const int col = half * 32;
+    bool ok = true;
+    for (int j = 0; j < nkb && ok; ++j) {
+      const int pb = j & 1;
+      const uint32_t ph = (j >> 1) & 1;
+      ok = __all_sync(0xffffffff, mbar_wait(&s_full[pb], ph, status, kTimeoutTmemFull) &&
+                                      mbar_wait(&ds_free[pb], ph ^ 1, status, kTimeoutTmemFull));
+      if (!ok) break;
+      tc_fence_after();
+      float sv[32], dp[32];
+      tmem_ld32x2_sync(tS + pb * 64 + col + lane_off, tDP + pb * 64 + col + lane_off, sv, dp);
+      tc_fence_before();
+      mbar_arrive(&s_free[pb]);
+#pragma unroll
+      for (int t = 0; t < 32; ++t) {
+        const int kk = j * BK + col + t;
+        const float p = (kk > q) ? 0.f : exp2f(sv[t] * scale_log2 - lq);
+        dp[t] = p * (dp[t] - dq_i);
+      }
+      store_p_quarter(sDS + pb * C::kSTile, r, half, dp);
+      fence_proxy_async_smem();
+      mbar_arrive(&p_full[pb]);
+    }
+    if (__all_sync(0xffffffff, ok && mbar_wait(fin, 0, status, kTimeoutTmemFull))) {
+      tc_fence_after();
+      __nv_bfloat16* qrow = dqkv + (static_cast<size_t>(row0 + q) * H + h) * 3 * D + half * (D / 2);
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        float v[32];
+        tmem_ld32_sync(tDQ + half * (D / 2) + c * 32 + lane_off, v);
+        store_row_bf16(qrow + c * 32, v, scale);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 }  // namespace attn_tc
 }  // namespace dst
 
 using namespace dst;
 
 // Forward on the tensor-core path; T must be a multiple of 128.
-std::vector<at::Tensor> flash_attn_fwd_tc(const at::Tensor& qkv, int64_t H, int64_t D) {
+// mode: 0 = choose, 1 = ping-pong kernel (two query tiles per CTA), 2 = one tile per CTA.
+std::vector<at::Tensor> flash_attn_fwd_tc(const at::Tensor& qkv, int64_t H, int64_t D, int64_t mode) {
   TORCH_CHECK(qkv.is_cuda() && qkv.scalar_type() == at::kBFloat16 && qkv.dim() == 3 && qkv.is_contiguous(),
               "attention: contiguous bf16 [B, T, 3 H D] qkv required");
   TORCH_CHECK(D == 64 || D == 128, "attention: head_dim must be 64 or 128");
@@ -767,9 +1456,30 @@ std::vector<at::Tensor> flash_attn_fwd_tc(const at::Tensor& qkv, int64_t H, int6
   at::Tensor lse = at::empty({B, H, T}, qkv.options().dtype(at::kFloat));
   const float scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(D)));
   CUtensorMap tm = make_tmap_bf16(qkv.data_ptr(), 3 * H * D, static_cast<uint64_t>(B) * T, 3 * H * D, 64, 128);
-  dim3 grid(T / 128, H, B);
   auto st = at::cuda::getCurrentCUDAStream();
   auto* o = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  // Two query tiles per CTA when that still gives at least two CTAs per SM
+  // to schedule; otherwise one tile per CTA keeps more SMs busy.
+  const long pp_ctas = static_cast<long>(T / 256) * H * B;
+  const bool pingpong = (mode == 1) || (mode == 0 && T % 256 == 0 && pp_ctas >= 2L * num_sms());
+  if (pingpong) {
+    TORCH_CHECK(T % 256 == 0, "attention (ping-pong): T must be a multiple of 256");
+    dim3 grid2(T / 256, H, B);
+    if (D == 64) {
+      auto k = attn_tc::fwd_pp_kernel<64>;
+      constexpr int smem = attn_tc::PPCfg<64>::kSmem;
+      C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      k<<<grid2, attn_tc::kThreads, smem, st>>>(tm, o, lse.data_ptr<float>(), T, H, scale_log2, status_ptr());
+    } else {
+      auto k = attn_tc::fwd_pp_kernel<128>;
+      constexpr int smem = attn_tc::PPCfg<128>::kSmem;
+      C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      k<<<grid2, attn_tc::kThreads, smem, st>>>(tm, o, lse.data_ptr<float>(), T, H, scale_log2, status_ptr());
+    }
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return {out, lse};
+  }
+  dim3 grid(T / 128, H, B);
   if (D == 64) {
     auto k = attn_tc::fwd_tc_kernel<64>;
     constexpr int smem = attn_tc::Cfg<64>::kSmem;
@@ -787,8 +1497,9 @@ std::vector<at::Tensor> flash_attn_fwd_tc(const at::Tensor& qkv, int64_t H, int6
 
 
 // Backward on the tensor-core path; T must be a multiple of 128.
+// mode: 0 = double-buffered kernels (64-wide inner blocks), 2 = the single-buffered kernels.
 at::Tensor flash_attn_bwd_tc(const at::Tensor& dout, const at::Tensor& qkv, const at::Tensor& out,
-                             const at::Tensor& lse, int64_t H, int64_t D) {
+                             const at::Tensor& lse, int64_t H, int64_t D, int64_t mode) {
   TORCH_CHECK(qkv.is_cuda() && qkv.scalar_type() == at::kBFloat16 && qkv.dim() == 3 && qkv.is_contiguous(),
               "attention bwd: contiguous bf16 qkv required");
   TORCH_CHECK(D == 64 || D == 128, "attention: head_dim must be 64 or 128");
@@ -803,9 +1514,16 @@ at::Tensor flash_attn_bwd_tc(const at::Tensor& dout, const at::Tensor& qkv, cons
   const float scale = static_cast<float>(sc), scale_log2 = static_cast<float>(sc * 1.4426950408889634);
   auto st = at::cuda::getCurrentCUDAStream();
   const int rows = B * T * static_cast<int>(H);
-  attn_tc::bwd_rowdot_kernel<<<(rows + 7) / 8, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
-                                                             reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()),
-                                                             di.data_ptr<float>(), rows, T, H, D);
+  {
+    const auto* dop = reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr());
+    const auto* op = reinterpret_cast<const __nv_bfloat16*>(out.data_ptr());
+    const int64_t threads = static_cast<int64_t>(rows) * (D / 8);
+    const int blocks = static_cast<int>((threads + 255) / 256);
+    if (D == 64)
+      attn_tc::bwd_rowdot_kernel<64><<<blocks, 256, 0, st>>>(dop, op, di.data_ptr<float>(), rows, T, H);
+    else
+      attn_tc::bwd_rowdot_kernel<128><<<blocks, 256, 0, st>>>(dop, op, di.data_ptr<float>(), rows, T, H);
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   const uint64_t nrows = static_cast<uint64_t>(B) * T;
   const int blk = (D == 64) ? 128 : 64;  // inner block: BQ of dK/dV, BK of dQ
@@ -817,6 +1535,33 @@ at::Tensor flash_attn_bwd_tc(const at::Tensor& dout, const at::Tensor& qkv, cons
   const float* l = lse.data_ptr<float>();
   const float* d = di.data_ptr<float>();
   dim3 grid(T / 128, H, B);
+  if (mode != 2) {  // double-buffered kernels (64-wide inner blocks)
+    CUtensorMap tmQKV64 = make_tmap_bf16(qkv.data_ptr(), 3 * H * D, nrows, 3 * H * D, 64, 64);
+    CUtensorMap tmDO64 = make_tmap_bf16(dout.data_ptr(), H * D, nrows, H * D, 64, 64);
+    if (D == 64) {
+      auto k1 = attn_tc::dkdv_db_kernel<64>;
+      constexpr int s1 = attn_tc::DkdvDbCfg<64>::kSmem;
+      C10_CUDA_CHECK(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, s1));
+      k1<<<grid, attn_tc::kThreads, s1, st>>>(tmQKV128, tmQKV64, tmDO64, l, d, dq, T, H, scale_log2, scale, status_ptr());
+      C10_CUDA_KERNEL_LAUNCH_CHECK();
+      auto k2 = attn_tc::dq_db_kernel<64>;
+      constexpr int s2 = attn_tc::DqDbCfg<64>::kSmem;
+      C10_CUDA_CHECK(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, s2));
+      k2<<<grid, attn_tc::kThreads, s2, st>>>(tmQKV128, tmDO128, tmQKV64, l, d, dq, T, H, scale_log2, scale, status_ptr());
+    } else {
+      auto k1 = attn_tc::dkdv_db_kernel<128>;
+      constexpr int s1 = attn_tc::DkdvDbCfg<128>::kSmem;
+      C10_CUDA_CHECK(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, s1));
+      k1<<<grid, attn_tc::kThreads, s1, st>>>(tmQKV128, tmQKV64, tmDO64, l, d, dq, T, H, scale_log2, scale, status_ptr());
+      C10_CUDA_KERNEL_LAUNCH_CHECK();
+      auto k2 = attn_tc::dq_db_kernel<128>;
+      constexpr int s2 = attn_tc::DqDbCfg<128>::kSmem;
+      C10_CUDA_CHECK(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, s2));
+      k2<<<grid, attn_tc::kThreads, s2, st>>>(tmQKV128, tmDO128, tmQKV64, l, d, dq, T, H, scale_log2, scale, status_ptr());
+    }
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return dqkv;
+  }
   if (D == 64) {
     auto k1 = attn_tc::dkdv_tc_kernel<64, 128>;
     constexpr int s1 = attn_tc::DkdvCfg<64, 128>::kSmem;
@@ -843,6 +1588,9 @@ at::Tensor flash_attn_bwd_tc(const at::Tensor& dout, const at::Tensor& qkv, cons
 }
 
 void register_attn_tc(pybind11::module& m) {
-  m.def("flash_attn_fwd_tc", &flash_attn_fwd_tc, "causal flash attention forward on tcgen05 (T % 128 == 0)");
-  m.def("flash_attn_bwd_tc", &flash_attn_bwd_tc, "causal flash attention backward on tcgen05 (T % 128 == 0)");
+  m.def("flash_attn_fwd_tc", &flash_attn_fwd_tc, "causal flash attention forward on tcgen05 (T % 128 == 0)",
+        pybind11::arg("qkv"), pybind11::arg("H"), pybind11::arg("D"), pybind11::arg("mode") = 0);
+  m.def("flash_attn_bwd_tc", &flash_attn_bwd_tc, "causal flash attention backward on tcgen05 (T % 128 == 0)",
+        pybind11::arg("dout"), pybind11::arg("qkv"), pybind11::arg("out"), pybind11::arg("lse"), pybind11::arg("H"),
+        pybind11::arg("D"), pybind11::arg("mode") = 0);
 }

@@ -71,17 +71,7 @@ static void launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
     configured[dev] = true;
   }
   static const PeerArgs none{};
-  if constexpr (GATHER == 1 && !A_MN) {
-    // CTAs wait on each other's copies: launch cooperatively so that every
-    // CTA of the grid is resident at once (one per SM).
-    const PeerArgs& pr = *pa;
-    void* args[] = {const_cast<CUtensorMap*>(&ta), const_cast<CUtensorMap*>(&tb), const_cast<CUtensorMap*>(&to),
-                    const_cast<CUtensorMap*>(&tx), const_cast<GemmParams*>(&p), const_cast<PeerArgs*>(&pr)};
-    C10_CUDA_CHECK(cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(kern), dim3(grid), dim3(kGemmThreads), args,
-                                               smem, st));
-  } else {
-    kern<<<grid, kGemmThreads, smem, st>>>(ta, tb, to, tx, p, pa ? *pa : none);
-  }
+  kern<<<grid, kGemmThreads, smem, st>>>(ta, tb, to, tx, p, pa ? *pa : none);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -441,7 +431,9 @@ std::vector<at::Tensor> tp_gemm(const at::Tensor& A, bool a_mn, const at::Tensor
   pa.seq_local = seq_local;
   pa.rows_local = rows_local;
   pa.epoch = static_cast<uint32_t>(epoch);
+  TORCH_CHECK(done.scalar_type() == at::kInt && done.numel() >= 2, "tp_gemm: done must hold 2 int32 counters");
   pa.done_ctas = reinterpret_cast<unsigned int*>(done.data_ptr<int32_t>());
+  pa.claim = pa.done_ctas + 1;
   for (int r = 0; r < tp; ++r) pa.flags[r] = reinterpret_cast<uint32_t*>(flags[r]);
 
   // Local operand maps (the gathered one is only a shape template).

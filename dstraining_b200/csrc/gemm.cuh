@@ -96,6 +96,7 @@ struct PeerArgs {
   CUtensorMap scatter[kMaxPeers];  // each rank's receive buffer [tp * rows_local, N]
   uint32_t* flags[kMaxPeers];      // each rank's flag words for this channel [kinds][8]
   unsigned int* done_ctas;         // this rank's CTA completion counter (self-resetting)
+  unsigned int* claim;             // gather mode: next copy chunk to claim (reset by the last CTA)
   int tp, rank;
   int seq;         // T (tokens per batch row of the gathered / scattered tensor)
   int seq_local;   // T / tp
@@ -425,13 +426,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp >= 6) {
     // ------------------------------------------------------------ copier
     // Gather mode: pull every remote row block of A into the local gather
-    // buffer once, source by source in processing order, 64-column chunks
-    // spread over the CTAs; each landed chunk bumps the block's counter.
+    // buffer once, source by source in processing order; each copier warp
+    // claims the next 64-column chunk from a launch-wide counter, so the
+    // copies progress with whichever CTAs are resident (the kernel never
+    // needs all of its CTAs on the GPU at once, e.g. next to NCCL kernels
+    // that occupy some SMs). Each landed chunk bumps its block's counter.
     if (kRowGather) {
       const int per_src = num_m / pa.tp;
       const int total = (pa.tp - 1) * per_src * pa.kchunks;
       uint32_t ready = 0;
-      for (int c = blockIdx.x; c < total; c += gridDim.x) {
+      for (;;) {
+        int c = 0;
+        if (lane == 0) c = static_cast<int>(atomicAdd(pa.claim, 1u));
+        c = __shfl_sync(0xffffffff, c, 0);
+        if (c >= total) break;
         const int mb = gather_mblock(pa, per_src + c / pa.kchunks, num_m);  // skip own blocks
         const int kc = c % pa.kchunks;
         int src, local;
@@ -657,6 +665,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const unsigned int prev = atomicAdd(pa.done_ctas, 1u);
     if (prev == gridDim.x - 1) {
       atomicExch(pa.done_ctas, 0u);
+      if (kRowGather) atomicExch(pa.claim, 0u);  // every copier warp has left its loop
       if (SCATTER) peer_publish(pa, kSWritten, pa.epoch);
       if (GATHER != 0) {
         // Peers may overwrite their shards only after everyone has read them.

@@ -46,7 +46,7 @@ class _Channel:
         self.tp = tp
         self.buf = PeerBuffer(nbytes, tp, device)
         self.flags = PeerBuffer(64 * 4, tp, device)
-        self.done = torch.zeros(1, dtype=torch.int32, device=device)
+        self.done = torch.zeros(2, dtype=torch.int32, device=device)  # CTA-done and copy-claim counters
         self.epoch = 0
         self.nbytes = nbytes
 

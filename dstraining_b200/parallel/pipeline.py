@@ -19,15 +19,22 @@ Communication is designed for NCCL, not ported from the reference:
   reference shares world-spanning channel groups between pipeline columns
   and blocks the host in ``recv``, which deadlocks interleaved x TP on NCCL,
   ``README.md:275-283``.)
-* Nothing blocks the host. Receives are posted ahead of time (the full
-  sequence of messages each link will deliver is known from the schedule);
-  the compute stream waits on a receive only right before the forward or
-  backward that consumes it. Sends are fire-and-forget on the link's stream;
-  their buffers are held until the end of ``train_step``.
+* Nothing blocks the host. Each receive is posted right before the forward
+  or backward that consumes it, and the compute stream (not the host) waits
+  on it. Sends are fire-and-forget on the link's stream; their buffers are
+  held until the end of ``train_step``. A receive is never outstanding
+  before this rank has sent everything the peer needs to reach the matching
+  send, so host-side synchronisation inside a step cannot close a cycle.
 * Communicators are created and warmed (one blocking send/recv per link)
   once at construction, every rank visiting every link in one global order,
   so lazy NCCL communicator init can never interleave with schedule
   traffic.
+* Kernels are loaded when the CUDA context is created
+  (``CUDA_MODULE_LOADING=EAGER``, set by importing ``dstraining_b200``):
+  with lazy loading the first launch of a kernel waits for the device to go
+  idle, which a stage holding an outstanding send or receive, or a fused
+  collective spinning on a peer's flag, may not do while its peer is stuck
+  the same way.
 
 Under sequence parallelism the boundary tensor is ``[mb, T/tp, C]``.
 The last stage scales each microbatch loss by ``1/m``; ``train_step``
@@ -37,6 +44,8 @@ and ``None`` elsewhere. Gradients accumulate on the stage's parameters.
 
 from __future__ import annotations
 
+import os
+import warnings
 from collections import deque
 from typing import Dict, List, Optional, Tuple
 
@@ -66,13 +75,25 @@ def _all_columns(pp: PPContext) -> List[List[int]]:
     return [[c + s * stride for s in range(pp.world)] for c in range(stride)]
 
 
+def _check_module_loading(device: torch.device) -> None:
+    """Receives are posted ahead of use, so a kernel's first launch must not
+    wait for the device to go idle (lazy module loading does)."""
+    if device.type == "cuda" and os.environ.get("CUDA_MODULE_LOADING", "LAZY").upper() != "EAGER":
+        warnings.warn(
+            "CUDA_MODULE_LOADING is not EAGER: a pipeline stage may deadlock on its first step "
+            "(set it before CUDA is initialised; importing dstraining_b200 first does this)",
+            RuntimeWarning,
+        )
+
+
 def _build_links(pp: PPContext, ring: bool, device: torch.device) -> None:
     """Create (once per process) the two-rank link communicators for every
     column, in one global order, and warm the ones this rank belongs to."""
+    _check_module_loading(device)
     p = pp.world
     me = dist.get_rank()
     hops = p if ring else p - 1
-    warm = torch.zeros(1, device=device)
+    new_keys = []
     for column in _all_columns(pp):
         for flow in ("fwd", "bwd"):
             for s in range(hops):
@@ -81,18 +102,21 @@ def _build_links(pp: PPContext, ring: bool, device: torch.device) -> None:
                 key = (flow, src, dst)
                 if key in _LINKS:
                     continue
-                pair = sorted({src, dst})
-                g = dist.new_group(pair)
-                _LINKS[key] = g
-                # A real send/recv (not a collective) so that the p2p
-                # communicator NCCL keeps per peer pair exists before any
-                # schedule posts receives ahead of time.
-                if me == src:
-                    dist.send(warm, dst=dst, group=g)
-                elif me == dst:
-                    dist.recv(warm, src=src, group=g)
-    if warm.is_cuda:
-        torch.cuda.current_stream().synchronize()
+                _LINKS[key] = dist.new_group(sorted({src, dst}))
+                new_keys.append(key)
+    # Every communicator exists before any traffic. Then one real send/recv
+    # per link (not a collective), in the same global order everywhere, so
+    # the p2p connection NCCL sets up per peer pair exists before a schedule
+    # posts receives ahead of time; each is completed before the next.
+    warm = torch.zeros(1, device=device)
+    for flow, src, dst in new_keys:
+        g = _LINKS[(flow, src, dst)]
+        if me == src:
+            dist.send(warm, dst=dst, group=g)
+        elif me == dst:
+            dist.recv(warm, src=src, group=g)
+        if warm.is_cuda and me in (src, dst):
+            torch.cuda.current_stream().synchronize()
 
 
 class _Link:
@@ -113,10 +137,16 @@ class _Link:
 
 
 class _RecvQueue:
-    """Receives for one incoming link, posted ahead of use (at most
-    ``depth`` outstanding) and handed out in FIFO order."""
+    """Receives for one incoming link, handed out in FIFO order. Each receive
+    is posted when its tensor is needed (``depth`` = 0): a receive posted
+    earlier is a kernel spinning on the device until the peer sends, and any
+    device-wide synchronisation on this rank in the meantime (an allocator
+    ``cudaFree``, a library handle's first use, an ``.item()``) would then
+    wait for a send the peer can only make after this rank continues. The
+    exposed transfer is one boundary tensor over NVLink (tens of
+    microseconds)."""
 
-    def __init__(self, link: Optional[_Link], count: int, shape, dtype, device, depth: int = 2):
+    def __init__(self, link: Optional[_Link], count: int, shape, dtype, device, depth: int = 0):
         self.link, self.remaining = link, count
         self.shape, self.dtype, self.device, self.depth = shape, dtype, device, depth
         self.posted: deque = deque()
@@ -128,6 +158,9 @@ class _RecvQueue:
             self.remaining -= 1
 
     def pop(self) -> torch.Tensor:
+        if not self.posted and self.link is not None and self.remaining:
+            self.posted.append(self.link.irecv(self.shape, self.dtype, self.device))
+            self.remaining -= 1
         work, buf = self.posted.popleft()
         work.wait()  # NCCL: a stream wait, not a host block
         self._top_up()

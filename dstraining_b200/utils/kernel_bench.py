@@ -76,20 +76,25 @@ def bench_gemm(t, m, n, k, layout, epi, warmup, iters):
     return ms, 2.0 * m * n * k / (ms * 1e-3) / 1e12
 
 
-def bench_attn(t, b, tl, h, d, direction, warmup, iters):
+def bench_attn(t, b, tl, h, d, direction, warmup, iters, mode=0):
     from dstraining_b200.ops import native
 
     lib = native.lib()
     qkv = bf(b, tl, 3 * h * d)
-    fwd = lib.flash_attn_fwd_tc if tl % 128 == 0 else lib.flash_attn_fwd  # the model's dispatch
+    if tl % 128 == 0:  # the model's dispatch (mode 0); 1 / 2 force the ping-pong / one-tile forward
+        fwd = lambda q, hh, dd: lib.flash_attn_fwd_tc(q, hh, dd, mode)  # noqa: E731
+    else:
+        fwd = lib.flash_attn_fwd
     out, lse = fwd(qkv, h, d)
     dout = bf(b, tl, h * d)
     if direction == "fwd":
         fn = lambda: fwd(qkv, h, d)  # noqa: E731
         flops = 4.0 * b * h * tl * tl * d / 2
     else:
-        bwd = lib.flash_attn_bwd_tc if tl % 128 == 0 else lib.flash_attn_bwd
-        fn = lambda: bwd(dout, qkv, out, lse, h, d)  # noqa: E731
+        if tl % 128 == 0:  # mode 0: double-buffered kernels; 2: single-buffered
+            fn = lambda: lib.flash_attn_bwd_tc(dout, qkv, out, lse, h, d, mode)  # noqa: E731
+        else:
+            fn = lambda: lib.flash_attn_bwd(dout, qkv, out, lse, h, d)  # noqa: E731
         flops = 10.0 * b * h * tl * tl * d / 2  # dV, dK, dQ, dP + the recomputed S
     ms = t.run(fn, warmup, iters)
     return ms, flops / (ms * 1e-3) / 1e12
@@ -156,6 +161,8 @@ def main():
     ap.add_argument("--rows", type=int, default=16384)
     ap.add_argument("--c", type=int, default=768)
     ap.add_argument("--dir", default="fwd")
+    ap.add_argument("--attn-mode", type=int, default=0,
+                    help="forward: 0 auto, 1 ping-pong, 2 one tile per CTA; backward: 0 double-buffered, 2 single")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=10)
     a = ap.parse_args()
@@ -168,7 +175,7 @@ def main():
         ms, tf = bench_gemm(t, a.m, a.n, a.k, a.layout, a.epi, a.warmup, a.iters)
         rows = [(f"gemm {a.layout} {a.epi}", f"{a.m}x{a.n}x{a.k}", ms, tf, "TFLOP/s")]
     elif a.op == "attn":
-        ms, tf = bench_attn(t, a.b, a.t, a.h, a.d, a.dir, a.warmup, a.iters)
+        ms, tf = bench_attn(t, a.b, a.t, a.h, a.d, a.dir, a.warmup, a.iters, a.attn_mode)
         rows = [(f"attention {a.dir}", f"b{a.b} t{a.t} h{a.h} d{a.d}", ms, tf, "TFLOP/s")]
     else:
         ms, gb = bench_ln(t, a.rows, a.c, a.dir, a.warmup, a.iters)

@@ -219,15 +219,39 @@ def test_flash_forward_tcgen05(B, T, H, D):
     assert _rel(out, out2) < 2e-2
 
 
+@pytest.mark.parametrize("B,T,H,D", [(2, 256, 4, 64), (1, 1024, 3, 128), (2, 1024, 12, 64), (1, 2048, 2, 128)])
+@pytest.mark.parametrize("growing", [False, True])
+def test_flash_forward_pingpong(B, T, H, D, growing):
+    """Two-tile ping-pong forward (O in TMEM, thresholded rescaling) vs the
+    fp32 reference and the one-tile kernel. ``growing`` scales keys up along
+    the sequence so that row maxima keep rising and rescales happen."""
+    lib = _lib()
+    qkv = _bf(B, T, 3 * H * D, seed=31)
+    if growing:
+        ramp = torch.linspace(1.0, 6.0, T, device=qkv.device).view(1, T, 1, 1)
+        v = qkv.view(B, T, H, 3, D).float()
+        v[:, :, :, 1] *= ramp
+        qkv = v.view(B, T, 3 * H * D).to(torch.bfloat16).contiguous()
+    out, lse = lib.flash_attn_fwd_tc(qkv, H, D, 1)
+    ref = _ref_attention(qkv, H, D)
+    assert _rel(out, ref) < 2e-2
+    out2, lse2 = lib.flash_attn_fwd_tc(qkv, H, D, 2)
+    assert (lse - lse2).abs().max().item() < 2e-2
+    assert _rel(out, out2) < 2e-2
+    assert lib.read_status(True) == 0
+
+
 @pytest.mark.parametrize("B,T,H,D", [(2, 128, 4, 64), (1, 512, 3, 128), (2, 1024, 12, 64), (1, 2048, 2, 128)])
-def test_flash_backward_tcgen05(B, T, H, D):
-    """tcgen05 backward vs the fp32 reference and the mma.sync backward;
-    bitwise deterministic across runs."""
+@pytest.mark.parametrize("mode", [0, 2])
+def test_flash_backward_tcgen05(B, T, H, D, mode):
+    """tcgen05 backward (double-buffered kernels: mode 0; single-buffered:
+    mode 2) vs the fp32 reference and the mma.sync backward; bitwise
+    deterministic across runs."""
     lib = _lib()
     qkv = _bf(B, T, 3 * H * D, seed=40)
     dout = _bf(B, T, H * D, seed=41)
     out, lse = lib.flash_attn_fwd_tc(qkv, H, D)
-    g = lib.flash_attn_bwd_tc(dout, qkv, out, lse, H, D)
+    g = lib.flash_attn_bwd_tc(dout, qkv, out, lse, H, D, mode)
     g_old = lib.flash_attn_bwd(dout, qkv, out, lse, H, D)
     qr = qkv.float().requires_grad_(True)
     _ref_attention(qr, H, D).backward(dout.float())
@@ -235,4 +259,5 @@ def test_flash_backward_tcgen05(B, T, H, D):
     for i, name in enumerate("qkv"):
         assert _rel(gv[..., i, :], gr[..., i, :]) < 3e-2, name
         assert _rel(gv[..., i, :], go[..., i, :]) < 3e-2, name
-    assert torch.equal(g, lib.flash_attn_bwd_tc(dout, qkv, out, lse, H, D))
+    assert torch.equal(g, lib.flash_attn_bwd_tc(dout, qkv, out, lse, H, D, mode))
+    assert lib.read_status(True) == 0

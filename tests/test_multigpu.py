@@ -21,7 +21,8 @@ def _torchrun(n, script, *args, timeout=420):
            f"--nproc-per-node={n}", "--master-addr=127.0.0.1", f"--master-port={29400 + os.getpid() % 500}",
            os.path.join(ROOT, script), *args]
     r = subprocess.run(cmd, env=env, cwd=ROOT, capture_output=True, text=True)
-    print(r.stdout[-4000:], r.stderr[-4000:])
+    errors = [ln for ln in r.stderr.splitlines() if "error" in ln.lower() and not ln.startswith("frame #")]
+    print(r.stdout[-4000:], "\n".join(errors[:20]), r.stderr[-2000:])
     assert r.returncode == 0
 
 
@@ -36,3 +37,26 @@ def test_tp_suite_2gpu_nccl():
 @pytest.mark.parametrize("sp", [True, False])
 def test_tp_fused_2gpu(sp):
     _torchrun(2, "tests/suites/tp_fused_suite.py", *(["--sp"] if sp else []))
+
+
+def test_pp_1f1b_2gpu_nccl():
+    """1F1B on NCCL: receives are posted ahead, so this also checks that no
+    first kernel launch waits on a spinning receive."""
+    _torchrun(2, "tests/suites/pp_suite.py", "--pp", "2", "--micro", "1", "--device", "cuda")
+
+
+def test_pp_interleaved_2gpu_nccl():
+    _torchrun(2, "tests/suites/pp_suite.py", "--pp", "2", "--chunks", "2", "--micro", "1", "--device", "cuda")
+
+
+def test_pp_interleaved_tp_4gpu_nccl():
+    """Interleaved pipeline x TP x SP on NCCL (the composition the reference
+    documents as deadlocking, ``README.md:275-283``)."""
+    _torchrun(4, "tests/suites/pp_suite.py", "--pp", "2", "--tp", "2", "--chunks", "2", "--micro", "1", "--sp",
+              "--device", "cuda")
+
+
+def test_dp_3d_8gpu_nccl():
+    """dp2 x pp2 x tp2, interleaved, SP, bucketed DP on NCCL."""
+    _torchrun(8, "tests/suites/dp_suite.py", "--dp", "2", "--pp", "2", "--tp", "2", "--chunks", "2", "--micro", "1",
+              "--sp", "--bucketed", "--device", "cuda")
