@@ -89,9 +89,7 @@ constexpr int kWritten = 1;
 __global__ void __launch_bounds__(256) fused_dp_adam_kernel(const __grid_constant__ DpArgs a) {
   __shared__ bool go;
   if (threadIdx.x == 0) {
-    // every CTA publishes (the same value), so no CTA depends on another
-    // CTA of this launch being resident
-    publish(a.flags, kReady, a.rank, a.n, a.epoch);
+    if (blockIdx.x == 0) publish(a.flags, kReady, a.rank, a.n, a.epoch);
     go = wait_all(a.flags[a.rank], kReady, a.n, a.epoch, a.status);
   }
   __syncthreads();
