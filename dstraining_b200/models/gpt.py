@@ -46,6 +46,7 @@ from ..ops.embedding import embed_tokens
 from ..ops.layernorm import LayerNorm
 from ..parallel.comm import gather_from_tp_region
 from ..parallel.topology import PP_SINGLE, PPContext, TPContext
+from ..utils import trace
 from .layers import ColumnParallelLinear, RowParallelLinear
 
 VOCAB_PAD_MULTIPLE = 128
@@ -216,8 +217,13 @@ class _StageBody(nn.Module):
         return embed_tokens(idx, self.wte.weight, self.wpe.weight, self.tp, self.config.sequence_parallel)
 
     def _run_blocks(self, x: torch.Tensor) -> torch.Tensor:
-        for block in self.blocks:
-            x = block(x)
+        if not trace.enabled():
+            for block in self.blocks:
+                x = block(x)
+            return x
+        for i, block in enumerate(self.blocks):
+            with trace.nvtx_range(f"block{i}"):
+                x = block(x)
         return x
 
     def finalize_grads(self) -> None:

@@ -30,6 +30,7 @@ from .parallel import topology
 from .parallel.dp import GradReducer, allreduce_gradients
 from .parallel.pipeline import Pipeline1F1B, PipelineInterleaved
 from .utils.data import SyntheticShard, TokenShard
+from .utils.trace import nvtx_range
 
 
 def add_args(p: argparse.ArgumentParser) -> argparse.ArgumentParser:
@@ -144,19 +145,23 @@ class Trainer:
 
     def step_device(self, idx: torch.Tensor, tgt: torch.Tensor) -> Optional[torch.Tensor]:
         self.opt.zero_grad(set_to_none=True)
-        if self.pipe is not None:
-            loss = self.pipe.train_step(idx, tgt)
+        with nvtx_range("forward_backward"):
+            if self.pipe is not None:
+                loss = self.pipe.train_step(idx, tgt)
+                if self.reducer is not None:
+                    self.reducer.reduce()
+            else:
+                _, loss = self.model(idx, tgt)
+                loss.backward()
+        with nvtx_range("dp_reduce"):
             if self.reducer is not None:
-                self.reducer.reduce()
-        else:
-            _, loss = self.model(idx, tgt)
-            loss.backward()
-        if self.reducer is not None:
-            self.reducer.finish()
-        elif self.dp.enabled and not self.fused_dp:
-            allreduce_gradients(self.model, self.dp)
-        self.model.finalize_grads()
-        self.opt.step()
+                self.reducer.finish()
+            elif self.dp.enabled and not self.fused_dp:
+                allreduce_gradients(self.model, self.dp)
+        with nvtx_range("finalize_grads"):
+            self.model.finalize_grads()
+        with nvtx_range("optimizer"):
+            self.opt.step()
         self.step_index += 1
         if self.heartbeat is not None:
             self.heartbeat.tick()
@@ -169,6 +174,15 @@ class Trainer:
         tgt = tgt.to(self.device, non_blocking=True)
         loss = self.step_device(idx, tgt)
         return None if loss is None else float(loss.detach().float().item())
+
+    def world_max(self, values) -> list:
+        """Element-wise max of a list of floats over every rank (a collective:
+        all ranks must call it together)."""
+        t = torch.tensor([float(v) for v in values], dtype=torch.float64,
+                         device=self.device if self.device.type == "cuda" else "cpu")
+        if dist.is_initialized() and dist.get_world_size() > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.tolist()
 
     def dp_mean_loss(self, loss: torch.Tensor) -> torch.Tensor:
         avg = loss.detach().float().clone()

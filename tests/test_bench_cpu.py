@@ -1,0 +1,48 @@
+"""bench.py's config table: every layout it offers is a valid process grid
+for its model (world size, divisibility rules of the schedules and layers),
+and the 8-GPU layouts are the ones BASELINE.json names."""
+
+import importlib.util
+import os
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _bench():
+    spec = importlib.util.spec_from_file_location("bench_under_test", os.path.join(ROOT, "bench.py"))
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[spec.name] = mod  # dataclasses resolve annotations through it
+    spec.loader.exec_module(mod)
+    return mod
+
+
+@pytest.mark.parametrize("n", [1, 2, 4, 8])
+def test_layouts_valid(n):
+    bench = _bench()
+    for name, cfg in bench.CONFIGS.items():
+        lay = cfg.layout(n)
+        if lay is None:
+            continue
+        assert lay["tp"] * lay["pp"] * lay["dp"] == n, (name, n, lay)
+        batch = cfg.batch(lay)
+        assert batch % cfg.micro == 0, (name, n)
+        m = batch // cfg.micro
+        assert cfg.heads % lay["tp"] == 0 and (4 * cfg.embd) % lay["tp"] == 0
+        assert cfg.block % lay["tp"] == 0
+        assert cfg.layers % (lay["pp"] * lay["chunks"]) == 0, (name, n)
+        if lay["chunks"] > 1:
+            assert m % lay["pp"] == 0, (name, n)  # interleaving needs m % p == 0
+
+
+def test_baseline_layouts():
+    bench = _bench()
+    c = bench.CONFIGS
+    assert c["c2"].layout(8) == dict(tp=1, pp=1, dp=8, chunks=1) and c["c2"].batch(c["c2"].layout(8)) == 16
+    assert c["c3"].layout(8) == dict(tp=8, pp=1, dp=1, chunks=1) and c["c3"].sp and c["c3"].recompute
+    assert c["c4"].layout(8) == dict(tp=2, pp=4, dp=1, chunks=2) and c["c4"].batch(c["c4"].layout(8)) == 32
+    lay5 = c["c5"].layout(8)
+    assert lay5 == dict(tp=2, pp=2, dp=2, chunks=1) and c["c5"].batch(lay5) * lay5["dp"] == 64
+    assert bench.parallelism_name(lay5) == "tp2xpp2xdp2"

@@ -87,6 +87,10 @@ def test_train_cli_all_axes_and_resume(tmp_path):
     assert launch(8, [train, "--steps", "6", "--resume", *common], timeout=540, env=env) == 0
     lines = open(tmp_path / "m.jsonl").read().splitlines()
     assert len(lines) == 6  # steps 0-3, then 4-5 after the resume
+    import json
+
+    rec = json.loads(lines[-1])
+    assert rec["step"] == 5 and rec["status"] == 0 and rec["step_ms_max"] > 0 and rec["tok_s"] > 0
 
 
 @pytest.mark.parametrize("n,args", [(2, ("--dp", "2")), (4, ("--dp", "2", "--tp", "2", "--sp")), (4, ("--dp", "4",))])

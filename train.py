@@ -8,7 +8,9 @@ parallelism, selective recompute and bf16 + fp32 master weights.
     torchrun --nproc_per_node 8 train.py --dp 8 --bf16 --vp --gpt2 --batch 16 --vocab 50304
 
 Same flags as the reference's ``train.py:29-58`` (plus ``--bucket-mb``,
-checkpointing and ``--jsonl``). Logs ``step N  loss X  T tok/s`` from the
+checkpointing, ``--heartbeat-timeout`` and ``--jsonl``, whose records carry
+the loss, tok/s, the device step time max over ranks, the peak memory and
+the kernels' status word). Logs ``step N  loss X  T tok/s`` from the
 last pipeline stage's tp0/dp0 rank; the loss is averaged over DP and the
 throughput is over the steps since the previous log line, measured with the
 device synchronised.
@@ -22,6 +24,7 @@ import time
 import torch
 import torch.distributed as dist
 
+from dstraining_b200.ops import native
 from dstraining_b200.trainer import Trainer, add_args
 from dstraining_b200.utils import checkpoint
 
@@ -57,12 +60,35 @@ def run(args):
         )
     sink = open(args.jsonl, "a") if (args.jsonl and tr.is_logger) else None
     cuda = tr.device.type == "cuda"
+    events = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) if cuda else None
     t_last, s_last = time.time(), start_step
     for step in range(start_step, args.steps):
         idx, tgt = tr.shard.get_batch(step, pin=cuda)
+        t_step = time.perf_counter()
+        if events:
+            events[0].record()
         loss = tr.step_device(idx.to(tr.device, non_blocking=True), tgt.to(tr.device, non_blocking=True))
+        if events:
+            events[1].record()
         last = step == args.steps - 1
-        if tr.pp.is_last and (step % args.log_every == 0 or last):
+        logging = step % args.log_every == 0 or last
+        record = None
+        if args.jsonl and logging:
+            # every rank: this step's device time (CPU: host time) and the
+            # kernels' status word, reduced to the max over all ranks
+            if events:
+                events[1].synchronize()
+                ms = events[0].elapsed_time(events[1])
+            else:
+                ms = (time.perf_counter() - t_step) * 1e3
+            status = 0
+            if cuda and native.available():
+                status = int(native.lib().read_status(False))
+            ms_max, status_max = tr.world_max([ms, status])
+            record = {"step_ms_max": round(ms_max, 3), "status": int(status_max)}
+            if cuda:
+                record["max_mem_gb"] = round(torch.cuda.max_memory_allocated(tr.device) / 2**30, 3)
+        if tr.pp.is_last and logging:
             avg = tr.dp_mean_loss(loss)
             if tr.is_logger:
                 value = avg.item()  # synchronises the device
@@ -70,7 +96,7 @@ def run(args):
                 tps = tr.tokens_per_step * (step + 1 - s_last) / max(now - t_last, 1e-9)
                 print(f"step {step:5d}  loss {value:.4f}  {tps:,.0f} tok/s", flush=True)
                 if sink:
-                    sink.write(json.dumps({"step": step, "loss": value, "tok_s": tps}) + "\n")
+                    sink.write(json.dumps({"step": step, "loss": value, "tok_s": tps, **(record or {})}) + "\n")
                     sink.flush()
                 t_last, s_last = now, step + 1
         if args.ckpt_dir and args.ckpt_every and (step + 1) % args.ckpt_every == 0 and not last:
