@@ -135,30 +135,6 @@ def allgather_rows(owner, role, tp: TPContext, shard2: torch.Tensor, seq: int) -
                                      tp.rank, ch.next_epoch(), shard2)
 
 
-def dw_gather_b(owner, role, tp: TPContext, dy2: torch.Tensor, x_shard2: torch.Tensor, seq: int, split: bool = True):
-    """dW [N_out, C] = dy^T . AG_tokens(x_shard): B gathered along K."""
-    ch = channel(owner, role, tp, x_shard2.numel() * 2, x_shard2.device)
-    shard = _publish_shard(ch, x_shard2)
-    tokens = dy2.shape[0]
-    res = native.lib().tp_gemm(
-        dy2, True, shard, True, dy2.shape[1], x_shard2.shape[1], tokens, EPI_PARTIAL_F32 if split else EPI_STORE,
-        MODE_GATHER_B, ch.buf.ptrs, ch.flags.ptrs, ch.done, tp.rank, seq, ch.next_epoch(),
-    )
-    return native.lib().splitk_reduce(res[0]) if split else res[0]
-
-
-def dw_gather_a(owner, role, tp: TPContext, dy_shard2: torch.Tensor, x2: torch.Tensor, seq: int):
-    """dW [N_out, K] = AG_tokens(dy_shard)^T . x: A gathered along K."""
-    ch = channel(owner, role, tp, dy_shard2.numel() * 2, dy_shard2.device)
-    shard = _publish_shard(ch, dy_shard2)
-    tokens = x2.shape[0]
-    res = native.lib().tp_gemm(
-        shard, True, x2, True, dy_shard2.shape[1], x2.shape[1], tokens, EPI_PARTIAL_F32, MODE_GATHER_A, ch.buf.ptrs,
-        ch.flags.ptrs, ch.done, tp.rank, seq, ch.next_epoch(),
-    )
-    return native.lib().splitk_reduce(res[0])
-
-
 # ---------------------------------------------------------------------- layers
 class _ColumnTP(torch.autograd.Function):
     """Column-parallel linear under TP. sequence mode: x [B, T/tp, C] -> y
