@@ -63,6 +63,8 @@ def add_args(p: argparse.ArgumentParser) -> argparse.ArgumentParser:
     p.add_argument("--ckpt-dir", default=None, help="directory for sharded checkpoints")
     p.add_argument("--ckpt-every", type=int, default=0, help="save every N steps (0: only at the end if --ckpt-dir)")
     p.add_argument("--resume", action="store_true", help="resume from the latest checkpoint in --ckpt-dir")
+    p.add_argument("--ckpt-async", action="store_true",
+                   help="write periodic checkpoints from a background thread (training continues)")
     p.add_argument("--jsonl", default=None, help="append per-step metrics (JSON lines) to this file")
     p.add_argument("--heartbeat-timeout", type=float, default=0.0,
                    help="abort when a peer makes no progress for this many seconds (0: off)")

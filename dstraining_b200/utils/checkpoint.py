@@ -8,6 +8,9 @@ Layout of one checkpoint (a directory per step)::
                                    model weights plus optimizer state
         COMPLETE                   written last by rank 0: the checkpoint is whole
 
+``save(..., background=True)`` returns after the tensors are copied to host
+memory and writes the files from a thread (see :class:`PendingSave`).
+
 Each (tp, pp) cell is written by its data-parallel rank 0 (DP replicas hold
 identical weights and optimizer state). Tensors are keyed by their GLOBAL
 name - the parameter name in the full single-process model (via
@@ -25,8 +28,10 @@ The reference has no checkpointing; this format is new.
 
 from __future__ import annotations
 
+import datetime
 import json
 import os
+import threading
 from typing import Dict, Optional
 
 import torch
@@ -88,7 +93,65 @@ def _optimizer_state(opt, params):
     return out, step
 
 
-def save(root: str, step: int, model: nn.Module, opt, tp, pp, dp, config, seed: int, extra: Optional[dict] = None) -> str:
+class PendingSave:
+    """Handle of a checkpoint being written in the background. ``wait()``
+    blocks until this rank's part is on disk (rank 0: until the whole
+    checkpoint is marked COMPLETE) and re-raises a writer error."""
+
+    def __init__(self, path: str, thread: Optional[threading.Thread] = None):
+        self.path = path
+        self._thread = thread
+        self.error: Optional[BaseException] = None
+
+    def wait(self) -> str:
+        if self._thread is not None:
+            self._thread.join()
+            self._thread = None
+        if self.error is not None:
+            raise RuntimeError(f"checkpoint {self.path} failed") from self.error
+        return self.path
+
+    def done(self) -> bool:
+        return self._thread is None or not self._thread.is_alive()
+
+
+def _snapshot(t: torch.Tensor, background: bool) -> torch.Tensor:
+    """Host copy of ``t``; a CPU tensor is copied only when the file is
+    written in the background (training would otherwise change it)."""
+    c = t.detach().cpu()
+    return c.clone() if background and c.data_ptr() == t.data_ptr() else c
+
+
+def _write_manifest(path, gathered, step, seed, opt_step, config, tp, pp, dp, extra) -> None:
+    merged = {}
+    for part in gathered:
+        if part and part.get("index"):
+            merged.update(part["index"])
+    manifest = {
+        "format": "dstraining_b200/sharded-v1",
+        "step": step,
+        "seed": seed,
+        "optimizer_step": opt_step,
+        "config": dict(vars(config)),
+        "topology": {"tp": tp.world, "pp": pp.world, "dp": dp.world},
+        "tensors": merged,
+        "extra": extra or {},
+    }
+    with open(os.path.join(path, "manifest.json"), "w") as f:
+        json.dump(manifest, f, indent=1, sort_keys=True)
+
+
+def save(root: str, step: int, model: nn.Module, opt, tp, pp, dp, config, seed: int, extra: Optional[dict] = None,
+         background: bool = False, timeout_s: float = 1800.0):
+    """Write a checkpoint of every rank's shard (collective: call on all ranks).
+
+    ``background=False`` returns the checkpoint path once it is complete.
+    ``background=True`` does the collective part (gathering sharded optimizer
+    state, exchanging the tensor index) and copies every tensor to host memory
+    before returning a :class:`PendingSave`; the files are then written by a
+    thread, and rank 0 marks the checkpoint COMPLETE after every writer has
+    reported through the rendezvous store - so training continues while the
+    disk writes run. Call ``wait()`` before the next save and before exit."""
     path = os.path.join(root, f"step_{step:08d}")
     rank = dist.get_rank() if dist.is_initialized() else 0
     if rank == 0:
@@ -106,43 +169,57 @@ def save(root: str, step: int, model: nn.Module, opt, tp, pp, dp, config, seed: 
         if d is not None:
             full[d] *= tp.world
         index[f"model/{g}"] = {"shape": full, "split_dim": d, "pp": pp.rank, "dtype": str(p.dtype)}
-        tensors[f"model/{g}"] = p.detach().cpu()
+        tensors[f"model/{g}"] = _snapshot(p, background)
         for kind, t in state.get(name, {}).items():
             index[f"{kind}/{g}"] = {"shape": full, "split_dim": d, "pp": pp.rank, "dtype": str(t.dtype)}
-            tensors[f"{kind}/{g}"] = t.detach().cpu()
-    if dp.rank == 0:
-        torch.save(tensors, os.path.join(path, f"shard_tp{tp.rank}_pp{pp.rank}.pt"))
-    # Gather every cell's index on rank 0 for the manifest.
+            tensors[f"{kind}/{g}"] = _snapshot(t, background)
+    writer = dp.rank == 0
+    shard_file = os.path.join(path, f"shard_tp{tp.rank}_pp{pp.rank}.pt")
+    # Every cell's index (tp0 of each stage speaks for it) and who writes a shard.
+    mine = {"writer": writer, "index": index if writer and tp.rank == 0 else None}
     gathered = [None] * (dist.get_world_size() if dist.is_initialized() else 1)
     if dist.is_initialized():
-        dist.all_gather_object(gathered, index if dp.rank == 0 and tp.rank == 0 else None)
+        dist.all_gather_object(gathered, mine)
     else:
-        gathered = [index]
-    if rank == 0:
-        merged = {}
-        for part in gathered:
-            if part:
-                merged.update(part)
-        manifest = {
-            "format": "dstraining_b200/sharded-v1",
-            "step": step,
-            "seed": seed,
-            "optimizer_step": opt_step,
-            "config": dict(vars(config)),
-            "topology": {"tp": tp.world, "pp": pp.world, "dp": dp.world},
-            "tensors": merged,
-            "extra": extra or {},
-        }
-        with open(os.path.join(path, "manifest.json"), "w") as f:
-            json.dump(manifest, f, indent=1, sort_keys=True)
-    if dist.is_initialized():
-        dist.barrier()
-    if rank == 0:
-        with open(os.path.join(path, "COMPLETE"), "w") as f:
-            f.write("ok\n")
-    if dist.is_initialized():
-        dist.barrier()
-    return path
+        gathered = [mine]
+    if not background:
+        if writer:
+            torch.save(tensors, shard_file)
+        if rank == 0:
+            _write_manifest(path, gathered, step, seed, opt_step, config, tp, pp, dp, extra)
+        if dist.is_initialized():
+            dist.barrier()
+        if rank == 0:
+            with open(os.path.join(path, "COMPLETE"), "w") as f:
+                f.write("ok\n")
+        if dist.is_initialized():
+            dist.barrier()
+        return path
+
+    writers = [r for r, part in enumerate(gathered) if part and part["writer"]]
+    store = dist.distributed_c10d._get_default_store() if dist.is_initialized() else None
+    key = f"dst/ckpt/{os.path.abspath(path)}"
+    handle = PendingSave(path)
+
+    def work():
+        try:
+            if writer:
+                torch.save(tensors, shard_file)
+            if store is not None:
+                store.set(f"{key}/{rank}", "ok")
+            if rank == 0:
+                _write_manifest(path, gathered, step, seed, opt_step, config, tp, pp, dp, extra)
+                if store is not None:
+                    store.wait([f"{key}/{r}" for r in writers], datetime.timedelta(seconds=timeout_s))
+                with open(os.path.join(path, "COMPLETE"), "w") as f:
+                    f.write("ok\n")
+        except BaseException as e:  # noqa: BLE001 - surfaced by wait()
+            handle.error = e
+
+    t = threading.Thread(target=work, name=f"dst-ckpt-{step}", daemon=False)
+    handle._thread = t
+    t.start()
+    return handle
 
 
 def latest(root: str) -> Optional[str]:

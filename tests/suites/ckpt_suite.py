@@ -47,6 +47,7 @@ def main():
     ap.add_argument("--pp", type=int, default=1)
     ap.add_argument("--dir", required=True)
     ap.add_argument("--device", default="cpu")
+    ap.add_argument("--background", action="store_true", help="write the checkpoint from a thread")
     a = ap.parse_args()
     device = start(a.device)
     rep = Report()
@@ -60,7 +61,14 @@ def main():
 
     tr = trainer(a.tp, a.pp, seed=11, micro=micro)
     first = losses(tr, 3, 0)
-    path = checkpoint.save(a.dir, 3, tr.model, tr.opt, tr.tp, tr.pp, tr.dp, tr.config, 11)
+    if a.background:
+        pending = checkpoint.save(a.dir, 3, tr.model, tr.opt, tr.tp, tr.pp, tr.dp, tr.config, 11, background=True)
+        losses(tr, 2, 3)  # keep training while the files are written: the snapshot must not change
+        path = pending.wait()
+        dist.barrier()
+        rep.flag("background save marked complete", checkpoint.latest(a.dir) == path)
+    else:
+        path = checkpoint.save(a.dir, 3, tr.model, tr.opt, tr.tp, tr.pp, tr.dp, tr.config, 11)
     del tr
     tr2 = trainer(a.tp, a.pp, seed=11, micro=micro)  # same data stream
     with torch.no_grad():  # scramble the weights: the load must overwrite all of them

@@ -68,7 +68,8 @@ def test_recompute_suite():
     assert r.returncode == 0
 
 
-@pytest.mark.parametrize("n,args", [(2, ("--tp", "2")), (4, ("--tp", "2", "--pp", "2"))])
+@pytest.mark.parametrize("n,args", [(2, ("--tp", "2")), (4, ("--tp", "2", "--pp", "2")),
+                                    (4, ("--tp", "2", "--pp", "2", "--background"))])
 def test_checkpoint_suite(n, args, tmp_path):
     run(n, "ckpt_suite.py", *args, "--dir", str(tmp_path / "ckpt"))
 
@@ -83,7 +84,9 @@ def test_train_cli_all_axes_and_resume(tmp_path):
     common = ["--dp", "2", "--pp", "2", "--tp", "2", "--chunks", "2", "--sp", "--recompute", "--vp",
               "--micro", "1", "--batch", "4", "--device", "cpu", "--ckpt-dir", ck, "--jsonl", str(tmp_path / "m.jsonl"),
               "--heartbeat-timeout", "120"]  # healthy job: the watchdog must not fire
-    assert launch(8, [train, "--steps", "4", *common], timeout=540, env=env) == 0
+    assert launch(8, [train, "--steps", "4", "--ckpt-every", "2", "--ckpt-async", *common], timeout=540, env=env) == 0
+    assert sorted(os.listdir(ck)) == ["step_00000002", "step_00000004"]
+    assert all(os.path.exists(os.path.join(ck, d, "COMPLETE")) for d in os.listdir(ck))
     assert launch(8, [train, "--steps", "6", "--resume", *common], timeout=540, env=env) == 0
     lines = open(tmp_path / "m.jsonl").read().splitlines()
     assert len(lines) == 6  # steps 0-3, then 4-5 after the resume

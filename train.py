@@ -62,6 +62,7 @@ def run(args):
     cuda = tr.device.type == "cuda"
     events = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) if cuda else None
     t_last, s_last = time.time(), start_step
+    pending = None  # checkpoint being written in the background
     for step in range(start_step, args.steps):
         idx, tgt = tr.shard.get_batch(step, pin=cuda)
         t_step = time.perf_counter()
@@ -100,7 +101,13 @@ def run(args):
                     sink.flush()
                 t_last, s_last = now, step + 1
         if args.ckpt_dir and args.ckpt_every and (step + 1) % args.ckpt_every == 0 and not last:
-            checkpoint.save(args.ckpt_dir, step + 1, tr.model, tr.opt, tr.tp, tr.pp, tr.dp, tr.config, args.seed)
+            if pending is not None:
+                pending.wait()  # one background write at a time
+            out = checkpoint.save(args.ckpt_dir, step + 1, tr.model, tr.opt, tr.tp, tr.pp, tr.dp, tr.config,
+                                  args.seed, background=args.ckpt_async)
+            pending = out if args.ckpt_async else None
+    if pending is not None:
+        pending.wait()
     if args.ckpt_dir:
         checkpoint.save(args.ckpt_dir, args.steps, tr.model, tr.opt, tr.tp, tr.pp, tr.dp, tr.config, args.seed)
     if sink:
