@@ -15,7 +15,8 @@ Three layers, none of which needs a GPU fault to be exercised:
   process-group timeout, and the launcher sees the job fail.
 
 ``report_failure(reason)`` lets a rank that catches an exception tell its
-peers before it exits. Device-side waits are bounded inside the kernels
+peers before it exits. :class:`StepGate` checks, on the host and before a
+step launches anything, that every rank has reached that step. Device-side waits are bounded inside the kernels
 (status word, see ``read_status``); this module covers ranks.
 
 The reference has no failure handling (its only guard is
@@ -24,6 +25,7 @@ The reference has no failure handling (its only guard is
 
 from __future__ import annotations
 
+import datetime
 import os
 import sys
 import threading
@@ -159,6 +161,40 @@ class Watchdog:
 
     def stop(self) -> None:
         self._stop.set()
+
+
+class StepGate:
+    """Host-side rendezvous at the start of every step, before any kernel or
+    collective of that step is launched: each rank posts ``step`` to the store
+    and waits (at most ``timeout`` seconds) until every rank has posted it.
+    A rank that left between steps (exited, crashed, hung on the host) is
+    therefore noticed by the others while none of their kernels or
+    collectives is in flight, and :meth:`enter` raises :class:`PeerFailure`
+    naming the missing ranks. Costs one store round trip per step."""
+
+    def __init__(self, timeout: float = 30.0, prefix: str = f"{_PREFIX}/gate"):
+        self.timeout = timeout
+        self.prefix = prefix
+        self.rank = dist.get_rank()
+        self.world = dist.get_world_size()
+
+    def _key(self, step: int, rank: int) -> str:
+        return f"{self.prefix}/{step}/{rank}"
+
+    def enter(self, step: int) -> None:
+        store = _store()
+        store.set(self._key(step, self.rank), "1")
+        keys = [self._key(step, r) for r in range(self.world)]
+        try:
+            store.wait(keys, datetime.timedelta(seconds=self.timeout))
+        except Exception as e:  # noqa: BLE001 - store timeout: name the missing ranks
+            missing = [r for r in range(self.world) if not store.check([keys[r]])]
+            raise PeerFailure(f"rank(s) {missing} did not reach step {step} within {self.timeout:.0f} s") from e
+        if step >= 2:  # every rank has passed step - 1, so nobody waits on step - 2 any more
+            try:
+                store.delete_key(self._key(step - 2, self.rank))
+            except Exception:  # noqa: BLE001 - stores without delete keep the key
+                pass
 
 
 def start_monitoring(interval: float = 1.0, timeout: float = 10.0):

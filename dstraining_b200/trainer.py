@@ -68,6 +68,9 @@ def add_args(p: argparse.ArgumentParser) -> argparse.ArgumentParser:
     p.add_argument("--jsonl", default=None, help="append per-step metrics (JSON lines) to this file")
     p.add_argument("--heartbeat-timeout", type=float, default=0.0,
                    help="abort when a peer makes no progress for this many seconds (0: off)")
+    p.add_argument("--step-gate-timeout", type=float, default=0.0,
+                   help="before each step, wait at most this long for every rank to reach it; "
+                        "raise PeerFailure otherwise (0: off)")
     return p
 
 
@@ -134,7 +137,11 @@ class Trainer:
         self.tokens_per_step = args.batch * cfg.block_size * args.dp
         self.is_logger = self.pp.is_last and self.tp.rank == 0 and self.dp.rank == 0
         self.step_index = 0
-        self.heartbeat = self.watchdog = None
+        self.heartbeat = self.watchdog = self.gate = None
+        if getattr(args, "step_gate_timeout", 0.0) and dist.is_initialized() and dist.get_world_size() > 1:
+            from .parallel.health import StepGate
+
+            self.gate = StepGate(timeout=args.step_gate_timeout)
         if getattr(args, "heartbeat_timeout", 0.0) and dist.is_initialized() and dist.get_world_size() > 1:
             from .parallel.health import start_monitoring
 
@@ -146,6 +153,8 @@ class Trainer:
         return sum(p.numel() for p in self.model.parameters())
 
     def step_device(self, idx: torch.Tensor, tgt: torch.Tensor) -> Optional[torch.Tensor]:
+        if self.gate is not None:
+            self.gate.enter(self.step_index)  # host side, before this step launches anything
         self.opt.zero_grad(set_to_none=True)
         with nvtx_range("forward_backward"):
             if self.pipe is not None:

@@ -60,3 +60,21 @@ def test_dp_3d_8gpu_nccl():
     """dp2 x pp2 x tp2, interleaved, SP, bucketed DP on NCCL."""
     _torchrun(8, "tests/suites/dp_suite.py", "--dp", "2", "--pp", "2", "--tp", "2", "--chunks", "2", "--micro", "1",
               "--sp", "--bucketed", "--device", "cuda")
+
+
+def test_step_gate_2gpu(tmp_path):
+    """A rank leaves between steps of bf16 training with the fused NVLink DP
+    optimizer; the survivor notices on the host before launching its next
+    step (no kernel or collective waits for the departed rank). Plain peer
+    loads/stores only; NVLS off."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    marker = str(tmp_path / "g")
+    env = dict(os.environ, DST_PG_TIMEOUT_S="120", NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={29400 + os.getpid() % 500}",
+           os.path.join(ROOT, "tests/suites/gate_suite.py"), "--device", "cuda", "--marker", marker]
+    r = subprocess.run(cmd, env=env, cwd=ROOT, capture_output=True, text=True)
+    print(r.stdout[-3000:], r.stderr[-2000:])
+    assert r.returncode not in (0, 124)  # failed on purpose, not by the outer timeout
+    assert open(f"{marker}.0").read().startswith("4 ")

@@ -116,3 +116,17 @@ def test_failure_detection(mode, tmp_path):
     assert rc != 0
     assert time.time() - t0 < 60
     assert any(os.path.exists(f"{marker}.{r}") for r in range(3)), "no rank detected the failure"
+
+
+def test_step_gate_detects_departed_rank(tmp_path):
+    """A rank exits cleanly between steps; the survivor's step gate raises
+    before the next step launches anything."""
+    import time
+
+    marker = str(tmp_path / "g")
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="1")
+    t0 = time.time()
+    rc = launch(2, [os.path.join(SUITES, "gate_suite.py"), "--marker", marker], timeout=120, env=env)
+    assert rc != 0
+    assert time.time() - t0 < 60
+    assert open(f"{marker}.0").read().startswith("4 ")  # rank 0 noticed at step 4
