@@ -124,6 +124,7 @@ class FusedDPAdam:
         self._step = 0
         self._stepped = False
         self.overlap = overlap
+        self.defer = False  # set while accumulating gradients over micro-batches
         if self.native:
             from ..parallel.symm import PeerBuffer
 
@@ -144,6 +145,8 @@ class FusedDPAdam:
                 p.grad.zero_()
 
     def _hook(self, p) -> None:
+        if self.defer:
+            return  # gradient accumulation: only the last micro-batch's backward launches buckets
         b, i = self._where[id(p)]
         if b.late:
             return  # staged in step(), after finalize_grads

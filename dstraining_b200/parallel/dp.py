@@ -102,6 +102,7 @@ class GradReducer:
     def __init__(self, module: nn.Module, dp: DPContext, *, bucket_bytes: int = 25 * 1024 * 1024, overlap: bool = True):
         self.dp = dp
         self.overlap = overlap and dp.enabled
+        self.defer = False  # set while accumulating gradients over micro-batches
         self.buckets: List[_Bucket] = []
         self._where: Dict[int, tuple] = {}
         if not dp.enabled:
@@ -117,6 +118,8 @@ class GradReducer:
                 p.register_post_accumulate_grad_hook(self._hook)
 
     def _hook(self, p: nn.Parameter) -> None:
+        if self.defer:
+            return  # gradient accumulation: only the last micro-batch's backward reduces
         b, i = self._where[id(p)]
         b.stage(i)
         b.filled.add(i)

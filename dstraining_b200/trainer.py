@@ -53,7 +53,9 @@ def add_args(p: argparse.ArgumentParser) -> argparse.ArgumentParser:
     p.add_argument("--vocab", type=int, default=512)
     p.add_argument("--data", default="synthetic", help="'synthetic' or a uint16 token file")
     p.add_argument("--batch", type=int, default=8, help="batch per DP replica")
-    p.add_argument("--micro", type=int, default=1, help="micro batch size (pipeline only)")
+    p.add_argument("--micro", type=int, default=1, help="micro batch size (pipelines; with --grad-accum also pp=1)")
+    p.add_argument("--grad-accum", action="store_true",
+                   help="without pipelining: split each batch into --micro-sized micro-batches and accumulate")
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--lr", type=float, default=3e-4)
     p.add_argument("--seed", type=int, default=1337)
@@ -134,6 +136,11 @@ class Trainer:
             self.shard = SyntheticShard(cfg.vocab_size, cfg.block_size, args.batch, seed=args.seed, dp=self.dp)
         else:
             self.shard = TokenShard(args.data, cfg.block_size, args.batch, seed=args.seed, dp=self.dp)
+        self.accum = 1
+        if getattr(args, "grad_accum", False) and self.pipe is None and args.micro < args.batch:
+            if args.batch % args.micro:
+                raise ValueError(f"batch {args.batch} not divisible by micro batch {args.micro}")
+            self.accum = args.batch // args.micro
         self.tokens_per_step = args.batch * cfg.block_size * args.dp
         self.is_logger = self.pp.is_last and self.tp.rank == 0 and self.dp.rank == 0
         self.step_index = 0
@@ -161,6 +168,8 @@ class Trainer:
                 loss = self.pipe.train_step(idx, tgt)
                 if self.reducer is not None:
                     self.reducer.reduce()
+            elif self.accum > 1:
+                loss = self._accumulate(idx, tgt)
             else:
                 _, loss = self.model(idx, tgt)
                 loss.backward()
@@ -177,6 +186,28 @@ class Trainer:
         if self.heartbeat is not None:
             self.heartbeat.tick()
         return loss
+
+    def _accumulate(self, idx: torch.Tensor, tgt: torch.Tensor) -> torch.Tensor:
+        """Forward/backward of ``accum`` micro-batches, gradients summed in
+        ``param.grad`` (each loss scaled by 1/accum). The DP reducer's and the
+        fused optimizer's hooks stay quiet until the last micro-batch, whose
+        backward then reduces the accumulated gradients bucket by bucket."""
+        hooked = [o for o in (self.reducer, self.opt) if hasattr(o, "defer")]
+        xs, ys = idx.split(self.args.micro), tgt.split(self.args.micro)
+        m = len(xs)
+        total = None
+        for i, (x, y) in enumerate(zip(xs, ys)):
+            for o in hooked:
+                o.defer = i < m - 1
+            try:
+                _, loss = self.model(x, y)
+                (loss / m).backward()
+            finally:
+                for o in hooked:
+                    o.defer = False
+            part = loss.detach() / m
+            total = part if total is None else total + part
+        return total
 
     def step(self, idx: torch.Tensor, tgt: torch.Tensor) -> Optional[float]:
         """End-to-end step from host tensors; returns the local loss (host

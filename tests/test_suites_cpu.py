@@ -130,3 +130,8 @@ def test_step_gate_detects_departed_rank(tmp_path):
     assert rc != 0
     assert time.time() - t0 < 60
     assert open(f"{marker}.0").read().startswith("4 ")  # rank 0 noticed at step 4
+
+
+@pytest.mark.parametrize("n", [1, 2])
+def test_grad_accumulation(n):
+    run(n, "accum_suite.py")
