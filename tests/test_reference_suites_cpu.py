@@ -56,3 +56,15 @@ def test_dst_resolves_to_this_repository(suites):
     out = subprocess.run([sys.executable, "-c", "import dst, os; print(os.path.dirname(dst.__file__))"],
                          cwd=str(suites), env=_env(), capture_output=True, text=True, check=True).stdout.strip()
     assert os.path.realpath(out) == os.path.realpath(os.path.join(ROOT, "dst"))
+
+
+def test_reference_train_script_runs_on_our_dst(tmp_path):
+    """The reference's train.py (copied next to nothing else, so ``dst`` is
+    this repository's) with every axis at once, as in its quick start."""
+    src = os.path.join(ROOT, "baseline", "_ref", "train.py")
+    if not os.path.exists(src):
+        pytest.skip("reference not installed under baseline/_ref")
+    shutil.copy(src, tmp_path / "train.py")
+    args = ["--dp", "2", "--tp", "2", "--pp", "2", "--chunks", "2", "--sp", "--vp", "--recompute", "--bf16",
+            "--micro", "2", "--steps", "4", "--data", "synthetic", "--device", "cpu"]
+    assert launch(8, [str(tmp_path / "train.py"), *args], timeout=600, env=_env()) == 0
