@@ -13,9 +13,9 @@ import os
 
 # Load every kernel when the CUDA context is created instead of at its first
 # launch. With lazy loading, the first launch of a kernel waits for the device
-# to go idle; a pipeline stage that has posted an NCCL receive ahead of time
-# (a kernel spinning until the peer sends), or a fused collective spinning on
-# a peer's flag, never goes idle while that peer is stuck in the same way, so
+# to go idle; a rank with an outstanding NCCL send or receive (a kernel
+# spinning until the peer takes part), or a fused collective spinning on a
+# peer's flag, never goes idle while that peer is stuck in the same way, so
 # both ranks would wait forever. Must be set before the context exists.
 os.environ.setdefault("CUDA_MODULE_LOADING", "EAGER")
 

@@ -76,8 +76,9 @@ def _all_columns(pp: PPContext) -> List[List[int]]:
 
 
 def _check_module_loading(device: torch.device) -> None:
-    """Receives are posted ahead of use, so a kernel's first launch must not
-    wait for the device to go idle (lazy module loading does)."""
+    """Sends are fire-and-forget (a kernel spinning until the peer receives),
+    so a kernel's first launch must not wait for the device to go idle (lazy
+    module loading does)."""
     if device.type == "cuda" and os.environ.get("CUDA_MODULE_LOADING", "LAZY").upper() != "EAGER":
         warnings.warn(
             "CUDA_MODULE_LOADING is not EAGER: a pipeline stage may deadlock on its first step "
@@ -107,7 +108,7 @@ def _build_links(pp: PPContext, ring: bool, device: torch.device) -> None:
     # Every communicator exists before any traffic. Then one real send/recv
     # per link (not a collective), in the same global order everywhere, so
     # the p2p connection NCCL sets up per peer pair exists before a schedule
-    # posts receives ahead of time; each is completed before the next.
+    # posts its first receive; each is completed before the next.
     warm = torch.zeros(1, device=device)
     for flow, src, dst in new_keys:
         g = _LINKS[(flow, src, dst)]
