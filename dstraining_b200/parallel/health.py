@@ -197,6 +197,26 @@ class StepGate:
                 pass
 
 
+def maybe_inject_fault(step: int) -> None:
+    """Host-side fault injection for recovery tests: with
+    ``DST_INJECT_FAULT="<rank>:<step>"`` that rank raises at the start of that
+    step. With ``DST_INJECT_FAULT_ONCE=<file>`` it does so only if the file
+    does not exist yet (and creates it), so a restarted job runs through."""
+    spec = os.environ.get("DST_INJECT_FAULT")
+    if not spec:
+        return
+    rank, at = (int(v) for v in spec.split(":"))
+    if dist.get_rank() != rank or step != at:
+        return
+    once = os.environ.get("DST_INJECT_FAULT_ONCE")
+    if once:
+        if os.path.exists(once):
+            return
+        with open(once, "w") as f:
+            f.write(f"rank {rank} step {step}\n")
+    raise RuntimeError(f"injected fault on rank {rank} at step {step}")
+
+
 def start_monitoring(interval: float = 1.0, timeout: float = 10.0):
     """Heartbeat + watchdog for this rank; returns both (call ``stop()``)."""
     hb = Heartbeat(interval).start()

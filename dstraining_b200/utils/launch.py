@@ -6,18 +6,25 @@ no sockets or hostname resolution; exits non-zero if any rank fails, and
 kills the survivors if one rank fails or the optional ``--timeout`` expires
 (a dead rank must not leave its peers waiting forever). The reference ships
 the same launcher as a shell script (``scripts/launch_local.sh``).
+
+Automatic restart (``--max-restarts K --restart-args "--resume"``): when the
+job fails, every rank is stopped and the whole job is launched again (a new
+rendezvous) with the restart arguments appended, up to K times - with
+``train.py --ckpt-dir ... --ckpt-every ...`` this resumes from the latest
+complete checkpoint, the recovery path after a rank failure.
 """
 
 from __future__ import annotations
 
 import argparse
 import os
+import shlex
 import signal
 import subprocess
 import sys
 import tempfile
 import time
-from typing import List, Optional
+from typing import List, Optional, Sequence
 
 
 def launch(nproc: int, argv: List[str], timeout: Optional[float] = None, env: Optional[dict] = None) -> int:
@@ -52,13 +59,29 @@ def launch(nproc: int, argv: List[str], timeout: Optional[float] = None, env: Op
     return 0 if all(c == 0 for c in codes) else 1
 
 
+def launch_with_restarts(nproc: int, argv: List[str], max_restarts: int = 0, restart_args: Sequence[str] = (),
+                         timeout: Optional[float] = None, env: Optional[dict] = None) -> int:
+    """:func:`launch`, relaunching the whole job after a failure (at most
+    ``max_restarts`` times) with ``restart_args`` appended. Returns 0 once an
+    attempt succeeds, 1 when every attempt failed."""
+    for attempt in range(max_restarts + 1):
+        args = list(argv) if attempt == 0 else [*argv, *[a for a in restart_args if a not in argv]]
+        if launch(nproc, args, timeout, env) == 0:
+            return 0
+        if attempt < max_restarts:
+            print(f"[dst launch] job failed; restart {attempt + 1} of {max_restarts}", file=sys.stderr, flush=True)
+    return 1
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--timeout", type=float, default=None)
+    ap.add_argument("--timeout", type=float, default=None, help="per attempt")
+    ap.add_argument("--max-restarts", type=int, default=0)
+    ap.add_argument("--restart-args", default="", help="arguments appended on restarts, e.g. \"--resume\"")
     ap.add_argument("nproc", type=int)
     ap.add_argument("argv", nargs=argparse.REMAINDER)
     a = ap.parse_args()
-    sys.exit(launch(a.nproc, a.argv, a.timeout))
+    sys.exit(launch_with_restarts(a.nproc, a.argv, a.max_restarts, shlex.split(a.restart_args), a.timeout))
 
 
 if __name__ == "__main__":

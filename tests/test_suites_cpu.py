@@ -135,3 +135,27 @@ def test_step_gate_detects_departed_rank(tmp_path):
 @pytest.mark.parametrize("n", [1, 2])
 def test_grad_accumulation(n):
     run(n, "accum_suite.py")
+
+
+def test_restart_from_checkpoint(tmp_path):
+    """A rank fails at step 3 (host-side injection, once); the launcher stops
+    the job and relaunches it with --resume; training continues from the step-2
+    checkpoint and ends bitwise identical to an uninterrupted run."""
+    import torch
+
+    from dstraining_b200.utils.launch import launch_with_restarts
+
+    root = os.path.dirname(SUITES)
+    train = os.path.join(os.path.dirname(root), "train.py")
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="1")
+    common = ["--dp", "2", "--layers", "2", "--heads", "4", "--embd", "64", "--block", "32", "--vocab", "256",
+              "--batch", "4", "--steps", "6", "--ckpt-every", "2", "--device", "cpu"]
+    assert launch(2, [train, *common, "--ckpt-dir", str(tmp_path / "ref")], timeout=300, env=env) == 0
+    once = tmp_path / "injected"
+    fenv = dict(env, DST_INJECT_FAULT="1:3", DST_INJECT_FAULT_ONCE=str(once))
+    rc = launch_with_restarts(2, [train, *common, "--ckpt-dir", str(tmp_path / "ck")], max_restarts=1,
+                              restart_args=["--resume"], timeout=300, env=fenv)
+    assert rc == 0 and once.exists()
+    a = torch.load(tmp_path / "ref" / "step_00000006" / "shard_tp0_pp0.pt")
+    b = torch.load(tmp_path / "ck" / "step_00000006" / "shard_tp0_pp0.pt")
+    assert a.keys() == b.keys() and all(torch.equal(a[k], b[k]) for k in a)

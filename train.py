@@ -25,6 +25,7 @@ import torch
 import torch.distributed as dist
 
 from dstraining_b200.ops import native
+from dstraining_b200.parallel.health import maybe_inject_fault
 from dstraining_b200.trainer import Trainer, add_args
 from dstraining_b200.utils import checkpoint
 
@@ -64,6 +65,7 @@ def run(args):
     t_last, s_last = time.time(), start_step
     pending = None  # checkpoint being written in the background
     for step in range(start_step, args.steps):
+        maybe_inject_fault(step)
         idx, tgt = tr.shard.get_batch(step, pin=cuda)
         t_step = time.perf_counter()
         if events:
