@@ -44,6 +44,7 @@ from ..ops.attention import causal_attention, core_attention  # noqa: F401  (re-
 from ..ops.cross_entropy import vocab_parallel_cross_entropy
 from ..ops.embedding import embed_tokens
 from ..ops.layernorm import LayerNorm
+from ..ops.recompute import recompute
 from ..parallel.comm import gather_from_tp_region
 from ..parallel.topology import PP_SINGLE, PPContext, TPContext
 from ..utils import trace
@@ -68,6 +69,9 @@ class GPTConfig:
     sequence_parallel: bool = False
     recompute_attention: bool = False
     vocab_parallel_loss: bool = False
+    # Full activation recompute (not in the reference): each block keeps only
+    # its input and re-runs its forward in backward.
+    recompute_blocks: bool = False
 
     def __post_init__(self):
         if self.dropout != 0.0:
@@ -217,13 +221,14 @@ class _StageBody(nn.Module):
         return embed_tokens(idx, self.wte.weight, self.wpe.weight, self.tp, self.config.sequence_parallel)
 
     def _run_blocks(self, x: torch.Tensor) -> torch.Tensor:
-        if not trace.enabled():
+        full = self.config.recompute_blocks and torch.is_grad_enabled()
+        if not trace.enabled() and not full:
             for block in self.blocks:
                 x = block(x)
             return x
         for i, block in enumerate(self.blocks):
             with trace.nvtx_range(f"block{i}"):
-                x = block(x)
+                x = recompute(block, x) if full else block(x)
         return x
 
     def finalize_grads(self) -> None:

@@ -42,6 +42,8 @@ def add_args(p: argparse.ArgumentParser) -> argparse.ArgumentParser:
     p.add_argument("--chunks", type=int, default=1, help="model chunks per rank (v > 1: interleaved)")
     p.add_argument("--sp", action="store_true", help="sequence parallelism")
     p.add_argument("--recompute", action="store_true", help="selective attention recompute")
+    p.add_argument("--recompute-blocks", action="store_true",
+                   help="full activation recompute: each block keeps only its input")
     p.add_argument("--bf16", action="store_true", help="bf16 params + fp32 master weights")
     p.add_argument("--vp", action="store_true", help="vocab-parallel (fused) cross-entropy")
     p.add_argument("--naive-dp", action="store_true", help="per-parameter blocking all-reduce")
@@ -93,6 +95,7 @@ class Trainer:
             sequence_parallel=args.sp,
             recompute_attention=args.recompute,
             vocab_parallel_loss=args.vp,
+            recompute_blocks=getattr(args, "recompute_blocks", False),
         )
         cfg = self.config
         if args.chunks > 1:

@@ -121,6 +121,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--sp", action="store_true")
     ap.add_argument("--recompute", action="store_true")
+    ap.add_argument("--recompute-blocks", action="store_true", help="full activation recompute of every block")
     ap.add_argument("--vp", action="store_true")
     ap.add_argument("--device", default=None)
     a = ap.parse_args()
@@ -132,7 +133,8 @@ def main():
     toy_split(rep, tp, device, sequence=False)
     if a.sp:
         toy_split(rep, tp, device, sequence=True)
-    model = GPT(replace(cfg, recompute_attention=a.recompute), tp, seed=SEED).to(device)
+    model = GPT(replace(cfg, recompute_attention=a.recompute, recompute_blocks=a.recompute_blocks), tp,
+                seed=SEED).to(device)
     ref = GPT(cfg, topology.SINGLE, seed=SEED).to(device)
     if a.sp and tp.enabled:
         seq_sharding(rep, tp, model, cfg, device)

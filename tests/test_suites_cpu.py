@@ -19,7 +19,8 @@ def run(n, script, *args, timeout=540):
     assert launch(n, [os.path.join(SUITES, script), "--device", "cpu", *args], timeout=timeout, env=env) == 0
 
 
-@pytest.mark.parametrize("args", [(), ("--sp",), ("--sp", "--recompute", "--vp"), ("--vp",)])
+@pytest.mark.parametrize("args", [(), ("--sp",), ("--sp", "--recompute", "--vp"), ("--vp",),
+                                  ("--sp", "--recompute-blocks", "--vp")])
 def test_tp_suite(args):
     run(2, "tp_suite.py", *args)
 
@@ -159,3 +160,34 @@ def test_restart_from_checkpoint(tmp_path):
     a = torch.load(tmp_path / "ref" / "step_00000006" / "shard_tp0_pp0.pt")
     b = torch.load(tmp_path / "ck" / "step_00000006" / "shard_tp0_pp0.pt")
     assert a.keys() == b.keys() and all(torch.equal(a[k], b[k]) for k in a)
+
+
+def test_block_recompute_single_process():
+    """Full-block recompute: bitwise-identical loss and gradients, fewer bytes
+    saved for backward."""
+    import torch
+
+    from dstraining_b200.models.gpt import GPT, GPTConfig
+    from dstraining_b200.parallel.topology import SINGLE
+
+    cfg = GPTConfig(vocab_size=256, block_size=32, n_layer=3, n_head=4, n_embd=64)
+    idx = torch.randint(0, 256, (4, 32), generator=torch.Generator().manual_seed(0))
+
+    def run(flag):
+        m = GPT(GPTConfig(**{**vars(cfg), "recompute_blocks": flag}), SINGLE, seed=1)
+        saved = [0]
+
+        def pack(t):
+            saved[0] += t.numel() * t.element_size()
+            return t
+
+        with torch.autograd.graph.saved_tensors_hooks(pack, lambda t: t):
+            _, loss = m(idx, idx)
+        loss.backward()
+        return loss, {n: p.grad for n, p in m.named_parameters()}, saved[0]
+
+    l0, g0, b0 = run(False)
+    l1, g1, b1 = run(True)
+    assert torch.equal(l0, l1)
+    assert all(torch.equal(g0[n], g1[n]) for n in g0)
+    assert b1 < b0 / 2, (b0, b1)
