@@ -28,7 +28,9 @@ The reference has no checkpointing; this format is new.
 
 from __future__ import annotations
 
+import argparse
 import datetime
+import hashlib
 import json
 import os
 import threading
@@ -115,6 +117,30 @@ class PendingSave:
         return self._thread is None or not self._thread.is_alive()
 
 
+def _sha256(path: str) -> str:
+    h = hashlib.sha256()
+    with open(path, "rb") as f:
+        for chunk in iter(lambda: f.read(1 << 22), b""):
+            h.update(chunk)
+    return h.hexdigest()
+
+
+def _write_shard(tensors: Dict[str, torch.Tensor], shard_file: str) -> None:
+    """The shard, then its SHA-256 next to it (``<shard>.sha256``)."""
+    torch.save(tensors, shard_file)
+    with open(shard_file + ".sha256", "w") as f:
+        f.write(_sha256(shard_file) + "\n")
+
+
+def verify_shard(shard_file: str) -> bool:
+    """True when the shard matches its recorded SHA-256 (or none was recorded)."""
+    rec = shard_file + ".sha256"
+    if not os.path.exists(rec):
+        return True
+    with open(rec) as f:
+        return f.read().strip() == _sha256(shard_file)
+
+
 def _snapshot(t: torch.Tensor, background: bool) -> torch.Tensor:
     """Host copy of ``t``; a CPU tensor is copied only when the file is
     written in the background (training would otherwise change it)."""
@@ -184,7 +210,7 @@ def save(root: str, step: int, model: nn.Module, opt, tp, pp, dp, config, seed: 
         gathered = [mine]
     if not background:
         if writer:
-            torch.save(tensors, shard_file)
+            _write_shard(tensors, shard_file)
         if rank == 0:
             _write_manifest(path, gathered, step, seed, opt_step, config, tp, pp, dp, extra)
         if dist.is_initialized():
@@ -204,7 +230,7 @@ def save(root: str, step: int, model: nn.Module, opt, tp, pp, dp, config, seed: 
     def work():
         try:
             if writer:
-                torch.save(tensors, shard_file)
+                _write_shard(tensors, shard_file)
             if store is not None:
                 store.set(f"{key}/{rank}", "ok")
             if rank == 0:
@@ -242,7 +268,10 @@ class _Reader:
     def _file(self, t: int, p: int) -> dict:
         key = f"shard_tp{t}_pp{p}.pt"
         if key not in self._cache:
-            self._cache[key] = torch.load(os.path.join(self.path, key), map_location="cpu", weights_only=True)
+            f = os.path.join(self.path, key)
+            if not verify_shard(f):
+                raise RuntimeError(f"checkpoint shard {f} does not match its recorded SHA-256")
+            self._cache[key] = torch.load(f, map_location="cpu", weights_only=True)
         return self._cache[key]
 
     def full(self, key: str) -> Optional[torch.Tensor]:
@@ -315,3 +344,48 @@ def load(path: str, model: nn.Module, opt, tp) -> dict:
                         "exp_avg_sq": eas.to(p.device, p.dtype).clone(),
                     }
     return rd.manifest
+
+
+def inspect(path: str) -> dict:
+    """Summary of a checkpoint directory: step, topology, tensor count and
+    bytes, and which shards are missing or fail their checksum."""
+    with open(os.path.join(path, "manifest.json")) as f:
+        man = json.load(f)
+    topo = man["topology"]
+    missing, corrupt, nbytes = [], [], 0
+    for t in range(topo["tp"]):
+        for p in range(topo["pp"]):
+            f = os.path.join(path, f"shard_tp{t}_pp{p}.pt")
+            if not os.path.exists(f):
+                missing.append(os.path.basename(f))
+                continue
+            nbytes += os.path.getsize(f)
+            if not verify_shard(f):
+                corrupt.append(os.path.basename(f))
+    return {
+        "path": path,
+        "step": man["step"],
+        "complete": os.path.exists(os.path.join(path, "COMPLETE")),
+        "topology": topo,
+        "tensors": len(man["tensors"]),
+        "bytes": nbytes,
+        "missing": missing,
+        "corrupt": corrupt,
+        "ok": not missing and not corrupt and os.path.exists(os.path.join(path, "COMPLETE")),
+    }
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser(description="inspect / verify a sharded checkpoint")
+    ap.add_argument("path", help="a step_XXXXXXXX directory, or a root (its latest complete checkpoint)")
+    a = ap.parse_args(argv)
+    path = a.path
+    if not os.path.exists(os.path.join(path, "manifest.json")):
+        path = latest(path) or path
+    info = inspect(path)
+    print(json.dumps(info, indent=1))
+    raise SystemExit(0 if info["ok"] else 1)
+
+
+if __name__ == "__main__":
+    main()
