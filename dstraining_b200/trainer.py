@@ -26,6 +26,7 @@ import torch.distributed as dist
 from .models.gpt import GPT, GPTChunks, GPTConfig, GPTStage
 from .optim.fused_dp import FusedDPAdam
 from .optim.precision import MasterWeightOptimizer
+from .optim.schedule import lr_at, set_lr
 from .parallel import topology
 from .parallel.dp import GradReducer, allreduce_gradients
 from .parallel.pipeline import Pipeline1F1B, PipelineInterleaved
@@ -60,6 +61,9 @@ def add_args(p: argparse.ArgumentParser) -> argparse.ArgumentParser:
                    help="without pipelining: split each batch into --micro-sized micro-batches and accumulate")
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--lr", type=float, default=3e-4)
+    p.add_argument("--lr-schedule", choices=["constant", "cosine"], default="constant")
+    p.add_argument("--warmup-steps", type=int, default=0, help="linear learning-rate warm-up")
+    p.add_argument("--min-lr", type=float, default=0.0, help="final rate of the cosine schedule")
     p.add_argument("--seed", type=int, default=1337)
     p.add_argument("--log-every", type=int, default=1)
     p.add_argument("--device", default=None, help="cuda|cpu (default: cuda if available)")
@@ -165,6 +169,10 @@ class Trainer:
     def step_device(self, idx: torch.Tensor, tgt: torch.Tensor) -> Optional[torch.Tensor]:
         if self.gate is not None:
             self.gate.enter(self.step_index)  # host side, before this step launches anything
+        a = self.args
+        if getattr(a, "lr_schedule", "constant") != "constant" or getattr(a, "warmup_steps", 0):
+            # before backward: the fused optimizer launches buckets during it
+            set_lr(self.opt, lr_at(self.step_index, a.lr, a.steps, a.warmup_steps, a.lr_schedule, a.min_lr))
         self.opt.zero_grad(set_to_none=True)
         with nvtx_range("forward_backward"):
             if self.pipe is not None:

@@ -50,6 +50,7 @@ def run(args):
         if path:
             manifest = checkpoint.load(path, tr.model, tr.opt, tr.tp)
             start_step = int(manifest["step"])
+            tr.step_index = start_step  # schedules and the step gate continue from here
             if tr.is_logger:
                 print(f"resumed from {path} at step {start_step}", flush=True)
     if tr.is_logger:
