@@ -243,6 +243,30 @@ class Pipeline1F1B:
         assert not stash
         return torch.stack(losses).sum() if self.pp.is_last else None
 
+    def eval_step(self, idx: torch.Tensor, targets: torch.Tensor):
+        """Forward-only pass over the microbatches (no stash, no backward): each
+        stage receives, runs and sends in microbatch order. Returns the mean loss
+        on the last stage, ``None`` elsewhere."""
+        b = idx.shape[0]
+        if b % self.micro_batch_size:
+            raise ValueError(f"batch {b} not divisible by micro batch {self.micro_batch_size}")
+        m = b // self.micro_batch_size
+        meta = (self.act_shape, self.act_dtype, self.act_device)
+        fwd_q = _RecvQueue(self.fwd_in, m, *meta)
+        sent: list = []
+        total = None
+        with torch.no_grad():
+            for x_i, y_i in zip(idx.split(self.micro_batch_size), targets.split(self.micro_batch_size)):
+                x = x_i if self.pp.is_first else fwd_q.pop()
+                if self.pp.is_last:
+                    _, loss = self.stage(x, y_i)
+                    total = loss / m if total is None else total + loss / m
+                else:
+                    self.fwd_out.isend(self.stage(x), sent)
+            for work, _ in sent:
+                work.wait()
+        return total
+
 
 class PipelineInterleaved:
     """Interleaved 1F1B over the ``v`` chunks of a :class:`GPTChunks`.
@@ -358,3 +382,50 @@ class PipelineInterleaved:
             work.wait()
         assert all(not q for q in stash) and fed in (0, m)
         return torch.stack(losses).sum() if self.pp.is_last else None
+
+    def eval_step(self, idx: torch.Tensor, targets: torch.Tensor):
+        """Forward-only pass of the interleaved schedule: every forward step in the
+        training order (chunk ``(i mod pv) div p``), no backward. Returns the mean
+        loss on the rank holding the last virtual stage, ``None`` elsewhere."""
+        b = idx.shape[0]
+        if b % self.micro_batch_size:
+            raise ValueError(f"batch {b} not divisible by micro batch {self.micro_batch_size}")
+        m = b // self.micro_batch_size
+        p, v = self.pp.world, self.v
+        if m % p:
+            raise ValueError(f"interleaving needs microbatches {m} divisible by stages {p}")
+        micro_idx = idx.split(self.micro_batch_size)
+        micro_tgt = targets.split(self.micro_batch_size)
+        tnm = m * v
+
+        def chunk(step: int) -> int:
+            return (step % (p * v)) // p
+
+        n_fwd_in = sum(1 for i in range(tnm) if not self._is_vfirst(chunk(i)))
+        meta = (self.act_shape, self.act_dtype, self.act_device)
+        fwd_q = _RecvQueue(self.fwd_in if p > 1 else None, n_fwd_in if p > 1 else 0, *meta)
+        local: deque = deque()
+        sent: list = []
+        total = None
+        fed = tgt = 0
+        with torch.no_grad():
+            for i in range(tnm):
+                c = chunk(i)
+                if self._is_vfirst(c):
+                    x = micro_idx[fed]
+                    fed += 1
+                else:
+                    x = fwd_q.pop() if p > 1 else local.popleft()
+                if self._is_vlast(c):
+                    _, loss = self.model.chunks[c](x, micro_tgt[tgt])
+                    tgt += 1
+                    total = loss / m if total is None else total + loss / m
+                else:
+                    out = self.model.chunks[c](x)
+                    if p > 1:
+                        self.fwd_out.isend(out, sent)
+                    else:
+                        local.append(out)
+            for work, _ in sent:
+                work.wait()
+        return total

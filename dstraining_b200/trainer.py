@@ -74,6 +74,10 @@ def add_args(p: argparse.ArgumentParser) -> argparse.ArgumentParser:
     p.add_argument("--ckpt-async", action="store_true",
                    help="write periodic checkpoints from a background thread (training continues)")
     p.add_argument("--jsonl", default=None, help="append per-step metrics (JSON lines) to this file")
+    p.add_argument("--eval-data", default=None,
+                   help="held-out uint16 token file ('synthetic': a separately seeded random stream)")
+    p.add_argument("--eval-every", type=int, default=0, help="evaluate every N steps (0: off)")
+    p.add_argument("--eval-batches", type=int, default=4, help="batches per evaluation")
     p.add_argument("--heartbeat-timeout", type=float, default=0.0,
                    help="abort when a peer makes no progress for this many seconds (0: off)")
     p.add_argument("--step-gate-timeout", type=float, default=0.0,
@@ -236,6 +240,36 @@ class Trainer:
         if dist.is_initialized() and dist.get_world_size() > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return t.tolist()
+
+    def eval_loss(self, batches: int) -> Optional[float]:
+        """Mean loss over ``batches`` held-out batches, forward only (pipelines
+        run their forward-only schedule), averaged over DP. A collective over
+        the whole job; returns the value on the last pipeline stage and
+        ``None`` elsewhere."""
+        a = self.args
+        if getattr(self, "_eval_shard", None) is None:
+            cfg, seed = self.config, a.seed + 7919  # a stream disjoint from the training batches
+            if a.eval_data in (None, "synthetic"):
+                self._eval_shard = SyntheticShard(cfg.vocab_size, cfg.block_size, a.batch, seed=seed, dp=self.dp)
+            else:
+                self._eval_shard = TokenShard(a.eval_data, cfg.block_size, a.batch, seed=seed, dp=self.dp)
+        was_training = self.model.training
+        self.model.eval()
+        total = None
+        try:
+            for i in range(batches):
+                x, y = self._eval_shard.get_batch(i)
+                x, y = x.to(self.device), y.to(self.device)
+                with torch.no_grad():
+                    loss = self.pipe.eval_step(x, y) if self.pipe is not None else self.model(x, y)[1]
+                if loss is not None:
+                    part = loss.detach().float() / batches
+                    total = part if total is None else total + part
+        finally:
+            self.model.train(was_training)
+        if not self.pp.is_last:
+            return None
+        return float(self.dp_mean_loss(total).item())
 
     def dp_mean_loss(self, loss: torch.Tensor) -> torch.Tensor:
         avg = loss.detach().float().clone()

@@ -191,3 +191,24 @@ def test_block_recompute_single_process():
     assert torch.equal(l0, l1)
     assert all(torch.equal(g0[n], g1[n]) for n in g0)
     assert b1 < b0 / 2, (b0, b1)
+
+
+def test_eval_matches_across_pipeline_layouts(tmp_path):
+    """--eval-every: held-out loss after 2 training steps is the same whether
+    the model runs in one piece, as a 1F1B pipeline or as an interleaved
+    pipeline (forward-only schedules)."""
+    import json
+
+    root = os.path.dirname(SUITES)
+    train = os.path.join(os.path.dirname(root), "train.py")
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="1")
+    common = ["--layers", "4", "--heads", "4", "--embd", "64", "--block", "32", "--vocab", "256", "--batch", "4",
+              "--micro", "2", "--steps", "2", "--eval-every", "2", "--eval-batches", "2", "--device", "cpu"]
+    out = {}
+    for name, n, extra in [("single", 1, []), ("1f1b", 2, ["--pp", "2"]), ("interleaved", 2, ["--pp", "2", "--chunks", "2"])]:
+        sink = tmp_path / f"{name}.jsonl"
+        assert launch(n, [train, *common, *extra, "--jsonl", str(sink)], timeout=300, env=env) == 0, name
+        evals = [json.loads(ln)["eval_loss"] for ln in open(sink) if "eval_loss" in ln]
+        assert len(evals) == 1, name
+        out[name] = evals[0]
+    assert abs(out["single"] - out["1f1b"]) < 1e-4 and abs(out["single"] - out["interleaved"]) < 1e-4, out

@@ -103,6 +103,13 @@ def run(args):
                     sink.write(json.dumps({"step": step, "loss": value, "tok_s": tps, **(record or {})}) + "\n")
                     sink.flush()
                 t_last, s_last = now, step + 1
+        if args.eval_every and ((step + 1) % args.eval_every == 0 or last):
+            ev = tr.eval_loss(args.eval_batches)  # every rank takes part
+            if tr.is_logger:
+                print(f"eval step {step:5d}  loss {ev:.4f}", flush=True)
+                if sink:
+                    sink.write(json.dumps({"step": step, "eval_loss": ev}) + "\n")
+                    sink.flush()
         if args.ckpt_dir and args.ckpt_every and (step + 1) % args.ckpt_every == 0 and not last:
             if pending is not None:
                 pending.wait()  # one background write at a time
