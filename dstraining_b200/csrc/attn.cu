@@ -568,6 +568,10 @@ at::Tensor flash_attn_bwd(const at::Tensor& dout, const at::Tensor& qkv, const a
                           int64_t H, int64_t D) {
   check_qkv(qkv, H, D);
   TORCH_CHECK(dout.is_contiguous() && out.is_contiguous() && dout.sizes() == out.sizes(), "attention bwd: dout/out");
+  TORCH_CHECK(out.dim() == 3 && out.size(0) == qkv.size(0) && out.size(1) == qkv.size(1) && out.size(2) == H * D &&
+                  out.scalar_type() == at::kBFloat16 && dout.scalar_type() == at::kBFloat16,
+              "attention bwd: bf16 out / dout [B, T, H * D] required");
+  TORCH_CHECK(lse.numel() == qkv.size(0) * H * qkv.size(1), "attention bwd: lse [B, H, T] required");
   c10::cuda::CUDAGuard g(qkv.device());
   const int B = qkv.size(0), T = qkv.size(1);
   at::Tensor dqkv = at::empty_like(qkv);

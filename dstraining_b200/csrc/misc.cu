@@ -222,7 +222,8 @@ std::vector<at::Tensor> embedding_bwd(const at::Tensor& dy, const at::Tensor& id
   TORCH_CHECK(dy.is_contiguous() && dy.dim() == 3 && dy.scalar_type() == at::kBFloat16, "embedding_bwd: dy");
   c10::cuda::CUDAGuard g(dy.device());
   const int B = dy.size(0), T = dy.size(1), C = dy.size(2);
-  TORCH_CHECK(idx.size(0) == B && idx.size(1) == T, "embedding_bwd: idx shape");
+  TORCH_CHECK(idx.dim() == 2 && idx.size(0) == B && idx.size(1) == T, "embedding_bwd: idx shape");
+  TORCH_CHECK(C % 8 == 0 && block >= T && vocab > 0, "embedding_bwd: C % 8 == 0 and block >= T required");
   auto st = at::cuda::getCurrentCUDAStream();
   at::Tensor dwte = at::zeros({vocab, C}, dy.options());
   at::Tensor dwpe = at::zeros({block, C}, dy.options());
@@ -288,6 +289,7 @@ void adam_master_step(const std::vector<at::Tensor>& params, const std::vector<a
 
 std::vector<at::Tensor> ce_merge_tiles(const at::Tensor& tmax, const at::Tensor& tsum) {
   TORCH_CHECK(tmax.scalar_type() == at::kFloat && tmax.is_contiguous() && tsum.sizes() == tmax.sizes(), "ce_merge");
+  TORCH_CHECK(tmax.is_cuda() && tmax.dim() == 2 && tsum.is_contiguous(), "ce_merge: [rows, tiles] fp32 statistics");
   c10::cuda::CUDAGuard g(tmax.device());
   const int M = tmax.size(0), tiles = tmax.size(1);
   at::Tensor m = at::empty({M}, tmax.options());
@@ -307,6 +309,8 @@ void ce_grad_inplace(at::Tensor& logits, const at::Tensor& lse, const at::Tensor
   c10::cuda::CUDAGuard g(logits.device());
   const int M = logits.size(0), N = logits.size(1);
   TORCH_CHECK(N % 8 == 0, "ce_grad: N must be a multiple of 8");
+  TORCH_CHECK(lse.is_contiguous() && lse.numel() == M && targets.is_contiguous() && targets.numel() == M,
+              "ce_grad: lse and targets must hold one contiguous value per logits row");
   dim3 grid((N / 8 + 127) / 128, M);
   ce_grad_inplace_kernel<<<grid, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), lse.data_ptr<float>(), targets.data_ptr<int64_t>(), M, N,

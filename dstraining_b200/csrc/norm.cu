@@ -201,6 +201,12 @@ std::vector<at::Tensor> layernorm_fwd(const at::Tensor& x, const at::Tensor& w, 
 std::vector<at::Tensor> layernorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
                                       const at::Tensor& mean, const at::Tensor& rstd) {
   TORCH_CHECK(dy.is_contiguous() && x.is_contiguous() && dy.sizes() == x.sizes(), "layernorm_bwd: shapes");
+  TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.scalar_type() == at::kBFloat16 && dy.scalar_type() == at::kBFloat16 &&
+                  w.scalar_type() == at::kBFloat16 && w.is_contiguous(),
+              "layernorm_bwd: bf16 dy / x [rows, C] and weight required");
+  TORCH_CHECK(w.numel() == x.size(1) && mean.numel() == x.size(0) && rstd.numel() == x.size(0) &&
+                  mean.is_contiguous() && rstd.is_contiguous(),
+              "layernorm_bwd: weight [C], mean and rstd [rows] required");
   c10::cuda::CUDAGuard g(x.device());
   const int rows = x.size(0), C = x.size(1);
   at::Tensor dx = at::empty_like(x);
