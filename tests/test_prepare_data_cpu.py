@@ -58,3 +58,28 @@ def test_tokenizer_json(tmp_path):
             val_frac=0.25, num_proc=2)
     train = np.fromfile(tmp_path / "o" / "train.bin", dtype=np.uint16)
     assert train.tolist() == [2, 3, 4, 2, 0] * 6
+
+
+def test_train_on_prepared_data(tmp_path):
+    """prepare_data -> train.py --data train.bin --eval-data val.bin on 2 gloo
+    ranks (data parallel); the held-out loss is logged."""
+    import sys
+
+    from dstraining_b200.utils.launch import launch
+
+    src = tmp_path / "corpus"
+    os.makedirs(src)
+    for i in range(60):
+        (src / f"d{i}.txt").write_text(("the quick brown fox jumps over the lazy dog %d. " % i) * 20)
+    prepare([str(src)], str(tmp_path / "data"), "bytes", val_frac=0.1, seed=0)
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sink = tmp_path / "m.jsonl"
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="1")
+    argv = [os.path.join(root, "train.py"), "--dp", "2", "--layers", "1", "--heads", "2", "--embd", "32",
+            "--block", "64", "--vocab", "257", "--batch", "4", "--steps", "4", "--device", "cpu",
+            "--data", str(tmp_path / "data" / "train.bin"), "--eval-data", str(tmp_path / "data" / "val.bin"),
+            "--eval-every", "2", "--jsonl", str(sink)]
+    assert launch(2, argv, timeout=300, env=env) == 0
+    recs = [json.loads(ln) for ln in open(sink)]
+    evals = [r["eval_loss"] for r in recs if "eval_loss" in r]
+    assert len(evals) == 2 and all(np.isfinite(evals))
