@@ -15,8 +15,10 @@ backend the group has (NCCL on GPUs, gloo on CPU). On CUDA bf16 the parallel
 linear layers do not call them; they fuse the collective into their GEMM
 kernels over NVLink peer memory (``dstraining_b200.ops.tp_fused``).
 
-Reduce-scatter is emulated on gloo (all-reduce + local slice), which is the
-CPU correctness path only.
+Gloo has no reduce-scatter: on gloo it is an all-to-all of the chunks
+followed by a local sum in rank order (half the bytes of the reference's
+all-reduce + slice emulation, ``dst/ops.py:102-118``); if the gloo build
+lacks all-to-all, all-reduce + slice is used. This is the CPU path only.
 """
 
 from __future__ import annotations
@@ -27,6 +29,7 @@ import torch.distributed as dist
 from .topology import TPContext
 
 SEQ_DIM = 1
+_GLOO_A2A: dict = {}  # whether this gloo build supports all_to_all_single (probed on first use)
 
 
 def _is_gloo(group) -> bool:
@@ -68,6 +71,18 @@ def reduce_scatter_dim(t: torch.Tensor, tp: TPContext, dim: int) -> torch.Tensor
         raise ValueError(f"dim {dim} of size {n} not divisible by tp {tp.world}")
     chunk = n // tp.world
     if _is_gloo(tp.group):
+        if _GLOO_A2A.get("ok", True):
+            try:
+                moved = t.movedim(dim, 0).contiguous()
+                recv = torch.empty_like(moved)
+                dist.all_to_all_single(recv, moved, group=tp.group)  # chunk j of recv comes from rank j
+                _GLOO_A2A["ok"] = True
+                out = recv.view(tp.world, chunk, *moved.shape[1:]).sum(0)  # fixed rank order
+                return out.movedim(0, dim).contiguous()
+            except RuntimeError:
+                if "ok" in _GLOO_A2A:
+                    raise  # worked before: a real failure, not a missing capability
+                _GLOO_A2A["ok"] = False
         return all_reduce_sum(t, tp).narrow(dim, tp.rank * chunk, chunk).contiguous()
     moved = t.movedim(dim, 0).contiguous()
     out = torch.empty((chunk, *moved.shape[1:]), dtype=t.dtype, device=t.device)

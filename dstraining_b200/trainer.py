@@ -137,7 +137,8 @@ class Trainer:
         elif args.bf16:
             self.opt = MasterWeightOptimizer(model.parameters(), lr=args.lr)
         else:
-            self.opt = torch.optim.Adam(model.parameters(), lr=args.lr)
+            # multi-tensor (foreach) Adam also on CPU, where PyTorch defaults to the per-tensor loop
+            self.opt = torch.optim.Adam(model.parameters(), lr=args.lr, foreach=True)
         self.reducer = None
         if self.dp.enabled and not args.naive_dp and not self.fused_dp:
             self.reducer = GradReducer(
