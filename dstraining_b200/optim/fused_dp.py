@@ -232,6 +232,33 @@ class FusedDPAdam:
             self._launch(self.buckets[self._next])
             self._next += 1
 
+    # -- protocol invariants ------------------------------------------------
+    def protocol_errors(self) -> List[str]:
+        """Host-side check of the NVLink signal protocol after the last step
+        (synchronises the device): every rank's flag words must show, for
+        every rank r of the group, ``ready[r] == written[r] == epoch`` (the
+        number of bucket launches, identical on all ranks), and the status
+        word must be clear. Returns the violations (empty when all hold);
+        collective over the DP group when it has several ranks."""
+        if not self.native:
+            return []
+        torch.cuda.synchronize(self.device)
+        n = self.dp.world
+        words = self.flags.local.view(torch.int32)[: 2 * 8].cpu().tolist()  # [kind][kMaxRanks] uint32 flags
+        ready, written = words[0:n], words[8 : 8 + n]
+        errs = []
+        if any(v != self.epoch for v in ready + written):
+            errs.append(f"rank {self.dp.rank}: ready {ready} / written {written} != epoch {self.epoch}")
+        if self.dp.enabled:
+            epochs = [None] * n
+            dist.all_gather_object(epochs, self.epoch, group=self.dp.group)
+            if len(set(epochs)) != 1:
+                errs.append(f"epochs differ across ranks: {epochs}")
+        status = int(native.lib().read_status(False))
+        if status:
+            errs.append(f"rank {self.dp.rank}: status word {status}")
+        return errs
+
     # -- state access (checkpoints) ----------------------------------------
     def full_state(self, p) -> Optional[dict]:
         """Gather the full fp32 master / moments of parameter ``p`` (collective

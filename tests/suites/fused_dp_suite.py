@@ -104,6 +104,8 @@ def main():
     if device.type == "cuda":
         from dstraining_b200.ops import native
 
+        errs = opt.protocol_errors()
+        rep.flag(f"signal protocol invariants {errs or 'hold'}", not errs, only_rank0=False)
         rep.flag("device status word clear", native.lib().read_status(True) == 0, only_rank0=False)
     rep.finish(device)
 
