@@ -60,6 +60,8 @@ COMP_BLOCK0 = 10
 
 @dataclass
 class GPTConfig:
+    """Model shape and parallel features (``dst/model.py:81-95``); d_ff is 4·n_embd."""
+
     vocab_size: int = 50257
     block_size: int = 1024
     n_layer: int = 12
@@ -91,6 +93,9 @@ def component_generator(seed: int, component: int) -> torch.Generator:
 
 
 class CausalSelfAttention(nn.Module):
+    """Fused head-major qkv (column-parallel), causal attention over the full
+    sequence, row-parallel projection (``dst/model.py:122-167``)."""
+
     def __init__(self, config: GPTConfig, tp: TPContext, generator: torch.Generator):
         super().__init__()
         if config.n_head % tp.world:
@@ -113,6 +118,8 @@ class CausalSelfAttention(nn.Module):
 
 
 class MLP(nn.Module):
+    """c_fc (column-parallel) -> tanh GELU -> c_proj (row-parallel) (``dst/model.py:170-189``)."""
+
     def __init__(self, config: GPTConfig, tp: TPContext, generator: torch.Generator):
         super().__init__()
         mode = "sequence" if config.sequence_parallel else "replicated"
@@ -131,6 +138,8 @@ class MLP(nn.Module):
 
 
 class Block(nn.Module):
+    """Pre-LN block: x + attn(ln_1(x)), then x + mlp(ln_2(x)) (``dst/model.py:192-203``)."""
+
     def __init__(self, config: GPTConfig, tp: TPContext, generator: torch.Generator):
         super().__init__()
         self.ln_1 = LayerNorm(config.n_embd)

@@ -52,6 +52,11 @@ def _draw_full(out_features: int, in_features: int, std: float, generator) -> to
 
 
 class ColumnParallelLinear(nn.Module):
+    """Linear layer whose output features are split over TP (``dst/layers.py:26-78``):
+    the full ``[out, in]`` weight is drawn from the caller's generator and the
+    row shard kept; input ``"replicated"`` (f) or ``"sequence"`` (g); optional
+    ``gather_output``; CUDA bf16 runs the fused NVLink GEMMs."""
+
     def __init__(
         self,
         in_features: int,
@@ -99,6 +104,11 @@ class ColumnParallelLinear(nn.Module):
 
 
 class RowParallelLinear(nn.Module):
+    """Linear layer whose input features are split over TP (``dst/layers.py:81-135``):
+    the column shard of the full weight is kept; output all-reduced (f̄) or
+    reduce-scattered along the sequence (ḡ), then the full bias (and an optional
+    residual) added."""
+
     def __init__(
         self,
         in_features: int,

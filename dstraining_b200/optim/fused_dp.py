@@ -91,6 +91,10 @@ class _Bucket:
 
 
 class FusedDPAdam:
+    """DP gradient averaging fused with fp32-master Adam (module docstring):
+    ZeRO-1 sharded optimizer state, one NVLink kernel per bucket launched from
+    backward hooks on CUDA, PyTorch collectives on gloo."""
+
     def __init__(
         self,
         model: torch.nn.Module,
@@ -138,6 +142,7 @@ class FusedDPAdam:
 
     # -- bookkeeping ------------------------------------------------------
     def zero_grad(self, set_to_none: bool = True) -> None:
+        """Clear (or zero) the parameters' gradients."""
         for p in self.model_params:
             if set_to_none:
                 p.grad = None
@@ -212,6 +217,8 @@ class FusedDPAdam:
 
     # -- optimizer API ------------------------------------------------------
     def step(self) -> None:
+        """Launch the buckets still pending (all of them for pipelines; the SP bucket
+        after ``finalize_grads``) and make the compute stream wait for the updates."""
         for b in self.buckets:
             if not b.launched:
                 for i in range(len(b.params)):
@@ -277,6 +284,8 @@ class FusedDPAdam:
         return out
 
     def load_full_state(self, p, master, exp_avg, exp_avg_sq, step: int) -> None:
+        """Install this rank's slice of a full fp32 master / moment tensor of ``p``
+        (checkpoint loading; any DP layout)."""
         b, i = self._where[id(p)]
         lo, hi = self.dp.rank * b.slice, (self.dp.rank + 1) * b.slice
         o0, o1 = b.offsets[i], b.offsets[i] + p.numel()

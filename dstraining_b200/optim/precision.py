@@ -28,6 +28,12 @@ from ..ops import native
 
 
 class MasterWeightOptimizer:
+    """bf16 model parameters with fp32 master copies and an inner ``torch.optim.Adam``
+    over the masters (``dst/precision.py:27-44``): ``step()`` upcasts the gradients,
+    updates the masters and copies them back to the bf16 parameters. On CUDA bf16
+    the whole update is one multi-tensor native kernel; ``model_params``,
+    ``master_params`` and ``inner.state`` stay available."""
+
     def __init__(self, params: Iterable[torch.nn.Parameter], **adam_kwargs):
         self.model_params: List[torch.nn.Parameter] = [p for p in params if p.requires_grad]
         self.master_params = [p.detach().clone().float().requires_grad_(False) for p in self.model_params]
@@ -38,6 +44,7 @@ class MasterWeightOptimizer:
         self._tables = None
 
     def zero_grad(self, set_to_none: bool = True) -> None:
+        """Clear the bf16 parameters' gradients (and the masters')."""
         for p in self.model_params:
             if set_to_none:
                 p.grad = None
@@ -53,6 +60,7 @@ class MasterWeightOptimizer:
         return st
 
     def step(self) -> None:
+        """One Adam step on the fp32 masters, then bf16 parameters = masters."""
         if self._native:
             self._native_step()
             return

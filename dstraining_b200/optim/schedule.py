@@ -28,6 +28,7 @@ def lr_at(step: int, base_lr: float, total_steps: int, warmup_steps: int = 0, sc
 
 
 def set_lr(opt, lr: float) -> None:
+    """Set the learning rate of any optimizer of this package (or a torch one)."""
     if hasattr(opt, "inner"):  # MasterWeightOptimizer
         opt = opt.inner
     if hasattr(opt, "param_groups"):

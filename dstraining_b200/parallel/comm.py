@@ -48,6 +48,7 @@ def all_reduce_sum(t: torch.Tensor, tp: TPContext) -> torch.Tensor:
 
 
 def all_gather_dim(t: torch.Tensor, tp: TPContext, dim: int) -> torch.Tensor:
+    """Concatenate every rank's ``t`` along ``dim`` (group order); one collective."""
     t = t.contiguous()
     if dim == 0 and not _is_gloo(tp.group):
         out = torch.empty((t.shape[0] * tp.world, *t.shape[1:]), dtype=t.dtype, device=t.device)
@@ -66,6 +67,7 @@ def all_gather_dim(t: torch.Tensor, tp: TPContext, dim: int) -> torch.Tensor:
 
 
 def reduce_scatter_dim(t: torch.Tensor, tp: TPContext, dim: int) -> torch.Tensor:
+    """Sum ``t`` over the group and keep this rank's equal slice along ``dim``."""
     n = t.shape[dim]
     if n % tp.world:
         raise ValueError(f"dim {dim} of size {n} not divisible by tp {tp.world}")
@@ -91,6 +93,7 @@ def reduce_scatter_dim(t: torch.Tensor, tp: TPContext, dim: int) -> torch.Tensor
 
 
 def local_slice(t: torch.Tensor, tp: TPContext, dim: int) -> torch.Tensor:
+    """This rank's equal slice of ``t`` along ``dim`` (no communication)."""
     chunk = t.shape[dim] // tp.world
     return t.narrow(dim, tp.rank * chunk, chunk).contiguous()
 
@@ -161,24 +164,30 @@ class _ScatterSeq(torch.autograd.Function):
 
 
 def copy_to_tp_region(x: torch.Tensor, tp: TPContext) -> torch.Tensor:
+    """f: identity forward, all-reduce of the gradient backward (``dst/ops.py:177-180``)."""
     return _CopyToTP.apply(x, tp) if tp.enabled else x
 
 
 def reduce_from_tp_region(x: torch.Tensor, tp: TPContext) -> torch.Tensor:
+    """f̄: all-reduce forward, identity backward (``dst/ops.py:183-186``)."""
     return _ReduceFromTP.apply(x, tp) if tp.enabled else x
 
 
 def gather_from_tp_region(x: torch.Tensor, tp: TPContext) -> torch.Tensor:
+    """All-gather along the last dimension forward, local slice backward (``dst/ops.py:189-192``)."""
     return _GatherLastDim.apply(x, tp) if tp.enabled else x
 
 
 def gather_along_seq(x: torch.Tensor, tp: TPContext) -> torch.Tensor:
+    """g: all-gather along the sequence forward, reduce-scatter backward (``dst/ops.py:159-162``)."""
     return _GatherSeq.apply(x, tp) if tp.enabled else x
 
 
 def reduce_scatter_along_seq(x: torch.Tensor, tp: TPContext) -> torch.Tensor:
+    """ḡ: reduce-scatter along the sequence forward, all-gather backward (``dst/ops.py:165-168``)."""
     return _ReduceScatterSeq.apply(x, tp) if tp.enabled else x
 
 
 def scatter_along_seq(x: torch.Tensor, tp: TPContext) -> torch.Tensor:
+    """Local sequence slice forward, all-gather backward (``dst/ops.py:171-174``)."""
     return _ScatterSeq.apply(x, tp) if tp.enabled else x

@@ -35,6 +35,7 @@ from .topology import DPContext
 
 
 def allreduce_gradients(module: nn.Module, dp: DPContext) -> None:
+    """Naive DP: one blocking all-reduce per gradient, then divide by the world (``dst/dp.py:43-49``)."""
     if not dp.enabled:
         return
     for p in module.parameters():
@@ -99,6 +100,13 @@ class _Bucket:
 
 
 class GradReducer:
+    """Bucketed, overlapped DP gradient averaging (``dst/dp.py:78-142``): parameters in
+    reverse order are packed into persistent flat buckets (~``bucket_bytes``); with
+    ``overlap`` a post-accumulate-grad hook launches a bucket's all-reduce as soon as
+    all its gradients exist; ``finish()`` waits, averages and exposes the buffers
+    as ``param.grad``. ``reduce()`` launches every bucket (pipeline path); ``defer``
+    silences the hooks while gradients are being accumulated."""
+
     def __init__(self, module: nn.Module, dp: DPContext, *, bucket_bytes: int = 25 * 1024 * 1024, overlap: bool = True):
         self.dp = dp
         self.overlap = overlap and dp.enabled

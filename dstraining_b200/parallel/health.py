@@ -42,6 +42,8 @@ def _store():
 
 
 class PeerFailure(RuntimeError):
+    """A peer rank stopped making progress, reported a failure, or missed a step gate."""
+
     pass
 
 

@@ -174,6 +174,11 @@ def _param_meta(module) -> Tuple[torch.dtype, torch.device]:
 
 
 class Pipeline1F1B:
+    """1F1B pipeline schedule over a :class:`GPTStage` (``dst/pipeline.py:52-176``):
+    ``train_step(idx, targets)`` runs ``batch / micro_batch_size`` microbatches and
+    returns the batch-mean loss on the last stage (``None`` elsewhere);
+    ``eval_step`` is the forward-only counterpart."""
+
     def __init__(self, stage, pp: PPContext, micro_batch_size: int, seq_len: int):
         cfg = stage.config
         self.stage, self.pp = stage, pp

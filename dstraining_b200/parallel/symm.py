@@ -22,6 +22,10 @@ from .topology import TPContext
 
 
 class PeerBuffer:
+    """Equal-sized device buffers on every rank of ``ctx``, each mapped into every
+    other rank (CUDA IPC); ``ptrs[r]`` is rank r's buffer as seen from here.
+    Collective: all ranks construct the same buffers in the same order."""
+
     def __init__(self, nbytes: int, ctx: TPContext, device: torch.device):
         lib = native.lib()
         self.ctx = ctx

@@ -127,6 +127,7 @@ def init_distributed(backend: Optional[str] = None, timeout_s: Optional[float] =
 
 
 def default_device() -> torch.device:
+    """CUDA device of this process when CUDA is available, else CPU (``dst/parallel.py:100-103``)."""
     if torch.cuda.is_available():
         return torch.device("cuda", torch.cuda.current_device())
     return torch.device("cpu")

@@ -87,6 +87,9 @@ def add_args(p: argparse.ArgumentParser) -> argparse.ArgumentParser:
 
 
 class Trainer:
+    """Builds grid, model, schedule, optimizer and reducer from ``train.py``-style
+    arguments (module docstring) and runs optimisation steps."""
+
     def __init__(self, args: argparse.Namespace):
         topology.init_distributed()
         self.args = args
@@ -172,6 +175,8 @@ class Trainer:
         return sum(p.numel() for p in self.model.parameters())
 
     def step_device(self, idx: torch.Tensor, tgt: torch.Tensor) -> Optional[torch.Tensor]:
+        """One optimisation step on device tensors ``idx`` / ``tgt`` of this replica's
+        batch; returns the (batch-mean) loss tensor on the last stage, else ``None``."""
         if self.gate is not None:
             self.gate.enter(self.step_index)  # host side, before this step launches anything
         a = self.args
@@ -273,6 +278,7 @@ class Trainer:
         return float(self.dp_mean_loss(total).item())
 
     def dp_mean_loss(self, loss: torch.Tensor) -> torch.Tensor:
+        """The loss averaged over the DP group (a collective; last-stage ranks)."""
         avg = loss.detach().float().clone()
         if self.dp.enabled:
             dist.all_reduce(avg, group=self.dp.group)

@@ -249,6 +249,7 @@ def save(root: str, step: int, model: nn.Module, opt, tp, pp, dp, config, seed: 
 
 
 def latest(root: str) -> Optional[str]:
+    """The newest COMPLETE checkpoint directory under ``root`` (or None)."""
     if not os.path.isdir(root):
         return None
     steps = sorted(d for d in os.listdir(root) if d.startswith("step_") and os.path.exists(os.path.join(root, d, "COMPLETE")))

@@ -32,6 +32,9 @@ def _maybe_pin(t: torch.Tensor, pin: bool) -> torch.Tensor:
 
 
 class TokenShard:
+    """Random windows of a flat uint16 token file (``dst/data.py:23-45``); targets
+    are inputs shifted by one; batches are a pure function of (seed, step, dp rank)."""
+
     def __init__(self, path: str, block_size: int, batch_size: int, seed: int = 0, dp: DPContext = DP_SINGLE):
         self.data = np.memmap(path, dtype=np.uint16, mode="r")
         if len(self.data) < block_size + 1:
@@ -47,6 +50,8 @@ class TokenShard:
 
 
 class SyntheticShard:
+    """Uniform-random token ids and targets (``dst/data.py:48-66``), seeded like TokenShard."""
+
     def __init__(self, vocab_size: int, block_size: int, batch_size: int, seed: int = 0, dp: DPContext = DP_SINGLE):
         self.vocab_size, self.block_size, self.batch_size, self.seed, self.dp = (
             vocab_size,

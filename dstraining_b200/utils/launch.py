@@ -28,6 +28,8 @@ from typing import List, Optional, Sequence
 
 
 def launch(nproc: int, argv: List[str], timeout: Optional[float] = None, env: Optional[dict] = None) -> int:
+    """Run ``nproc`` ranks of ``python argv``; 0 if every rank exits 0, else 1
+    (survivors are killed when one fails or the timeout expires)."""
     store_dir = tempfile.mkdtemp(prefix="dst_store_")
     store = os.path.join(store_dir, "store")
     procs = []
