@@ -86,6 +86,31 @@ def add_args(p: argparse.ArgumentParser) -> argparse.ArgumentParser:
     return p
 
 
+def parse_args(argv=None) -> argparse.Namespace:
+    """``train.py`` arguments; ``--config FILE.yaml`` supplies defaults for any
+    flag (keys are flag names, with ``-`` or ``_``), and flags given on the
+    command line take precedence."""
+    pre = argparse.ArgumentParser(add_help=False)
+    pre.add_argument("--config", default=None)
+    known, _ = pre.parse_known_args(argv)
+    p = add_args(argparse.ArgumentParser())
+    p.add_argument("--config", default=None, help="YAML file of flag defaults (command line wins)")
+    if known.config:
+        import yaml
+
+        with open(known.config) as f:
+            conf = yaml.safe_load(f) or {}
+        dests = {a.dest for a in p._actions}
+        defaults = {}
+        for k, v in conf.items():
+            d = str(k).replace("-", "_")
+            if d not in dests:
+                raise ValueError(f"{known.config}: unknown flag {k!r}")
+            defaults[d] = v
+        p.set_defaults(**defaults)
+    return p.parse_args(argv)
+
+
 class Trainer:
     """Builds grid, model, schedule, optimizer and reducer from ``train.py``-style
     arguments (module docstring) and runs optimisation steps."""

@@ -16,7 +16,6 @@ throughput is over the steps since the previous log line, measured with the
 device synchronised.
 """
 
-import argparse
 import json
 import sys
 import time
@@ -26,12 +25,12 @@ import torch.distributed as dist
 
 from dstraining_b200.ops import native
 from dstraining_b200.parallel.health import maybe_inject_fault
-from dstraining_b200.trainer import Trainer, add_args
+from dstraining_b200.trainer import Trainer, parse_args
 from dstraining_b200.utils import checkpoint
 
 
 def main():
-    args = add_args(argparse.ArgumentParser()).parse_args()
+    args = parse_args()
     try:
         run(args)
     except Exception as e:  # tell the peers before dying, so they stop waiting
