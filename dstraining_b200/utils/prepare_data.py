@@ -26,7 +26,7 @@ import argparse
 import json
 import os
 import random
-from multiprocessing import Pool
+from multiprocessing import get_context
 from typing import Iterable, List, Optional, Sequence, Tuple
 
 import numpy as np
@@ -126,7 +126,8 @@ def prepare(inputs: Sequence[str], out: str, tokenizer: str = "bytes", eot: str 
     counts = []
     for name, part in (("train", train_docs), ("val", val_docs)):
         if num_proc > 1:
-            with Pool(num_proc, initializer=_init_worker, initargs=(tokenizer, eot)) as pool:
+            # spawned workers: forking a process that already runs threads (torch) is unsafe
+            with get_context("spawn").Pool(num_proc, initializer=_init_worker, initargs=(tokenizer, eot)) as pool:
                 chunks = pool.map(_encode, part, chunksize=64)
         else:
             _init_worker(tokenizer, eot)

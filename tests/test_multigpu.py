@@ -77,4 +77,5 @@ def test_step_gate_2gpu(tmp_path):
     r = subprocess.run(cmd, env=env, cwd=ROOT, capture_output=True, text=True)
     print(r.stdout[-3000:], r.stderr[-2000:])
     assert r.returncode not in (0, 124)  # failed on purpose, not by the outer timeout
-    assert open(f"{marker}.0").read().startswith("4 ")
+    with open(f"{marker}.0") as f:
+        assert f.read().startswith("4 ")

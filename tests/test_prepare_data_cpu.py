@@ -80,6 +80,6 @@ def test_train_on_prepared_data(tmp_path):
             "--data", str(tmp_path / "data" / "train.bin"), "--eval-data", str(tmp_path / "data" / "val.bin"),
             "--eval-every", "2", "--jsonl", str(sink)]
     assert launch(2, argv, timeout=300, env=env) == 0
-    recs = [json.loads(ln) for ln in open(sink)]
+    recs = [json.loads(ln) for ln in sink.read_text().splitlines()]
     evals = [r["eval_loss"] for r in recs if "eval_loss" in r]
     assert len(evals) == 2 and all(np.isfinite(evals))

@@ -89,7 +89,7 @@ def test_train_cli_all_axes_and_resume(tmp_path):
     assert sorted(os.listdir(ck)) == ["step_00000002", "step_00000004"]
     assert all(os.path.exists(os.path.join(ck, d, "COMPLETE")) for d in os.listdir(ck))
     assert launch(8, [train, "--steps", "6", "--resume", *common], timeout=540, env=env) == 0
-    lines = open(tmp_path / "m.jsonl").read().splitlines()
+    lines = (tmp_path / "m.jsonl").read_text().splitlines()
     assert len(lines) == 6  # steps 0-3, then 4-5 after the resume
     import json
 
@@ -130,7 +130,8 @@ def test_step_gate_detects_departed_rank(tmp_path):
     rc = launch(2, [os.path.join(SUITES, "gate_suite.py"), "--marker", marker], timeout=120, env=env)
     assert rc != 0
     assert time.time() - t0 < 60
-    assert open(f"{marker}.0").read().startswith("4 ")  # rank 0 noticed at step 4
+    with open(f"{marker}.0") as f:
+        assert f.read().startswith("4 ")  # rank 0 noticed at step 4
 
 
 @pytest.mark.parametrize("n", [1, 2])
@@ -208,7 +209,7 @@ def test_eval_matches_across_pipeline_layouts(tmp_path):
     for name, n, extra in [("single", 1, []), ("1f1b", 2, ["--pp", "2"]), ("interleaved", 2, ["--pp", "2", "--chunks", "2"])]:
         sink = tmp_path / f"{name}.jsonl"
         assert launch(n, [train, *common, *extra, "--jsonl", str(sink)], timeout=300, env=env) == 0, name
-        evals = [json.loads(ln)["eval_loss"] for ln in open(sink) if "eval_loss" in ln]
+        evals = [json.loads(ln)["eval_loss"] for ln in sink.read_text().splitlines() if "eval_loss" in ln]
         assert len(evals) == 1, name
         out[name] = evals[0]
     assert abs(out["single"] - out["1f1b"]) < 1e-4 and abs(out["single"] - out["interleaved"]) < 1e-4, out
