@@ -11,7 +11,9 @@ Automatic restart (``--max-restarts K --restart-args "--resume"``): when the
 job fails, every rank is stopped and the whole job is launched again (a new
 rendezvous) with the restart arguments appended, up to K times - with
 ``train.py --ckpt-dir ... --ckpt-every ...`` this resumes from the latest
-complete checkpoint, the recovery path after a rank failure.
+complete checkpoint, the recovery path after a rank failure. With
+``--restart-nproc M`` (and layout flags in ``--restart-args``) the job comes
+back on M ranks: checkpoints are resharded on load.
 """
 
 from __future__ import annotations
@@ -62,13 +64,18 @@ def launch(nproc: int, argv: List[str], timeout: Optional[float] = None, env: Op
 
 
 def launch_with_restarts(nproc: int, argv: List[str], max_restarts: int = 0, restart_args: Sequence[str] = (),
-                         timeout: Optional[float] = None, env: Optional[dict] = None) -> int:
+                         timeout: Optional[float] = None, env: Optional[dict] = None,
+                         restart_nproc: Optional[int] = None) -> int:
     """:func:`launch`, relaunching the whole job after a failure (at most
-    ``max_restarts`` times) with ``restart_args`` appended. Returns 0 once an
-    attempt succeeds, 1 when every attempt failed."""
+    ``max_restarts`` times) with ``restart_args`` appended (later flags win, so
+    they may also change the layout, e.g. ``--resume --tp 1``) and, if given,
+    ``restart_nproc`` ranks - an elastic restart on fewer (or more) GPUs from
+    the reshardable checkpoint. Returns 0 once an attempt succeeds, 1 when
+    every attempt failed."""
     for attempt in range(max_restarts + 1):
-        args = list(argv) if attempt == 0 else [*argv, *[a for a in restart_args if a not in argv]]
-        if launch(nproc, args, timeout, env) == 0:
+        args = list(argv) if attempt == 0 else [*argv, *restart_args]
+        n = nproc if attempt == 0 or restart_nproc is None else restart_nproc
+        if launch(n, args, timeout, env) == 0:
             return 0
         if attempt < max_restarts:
             print(f"[dst launch] job failed; restart {attempt + 1} of {max_restarts}", file=sys.stderr, flush=True)
@@ -80,10 +87,12 @@ def main() -> None:
     ap.add_argument("--timeout", type=float, default=None, help="per attempt")
     ap.add_argument("--max-restarts", type=int, default=0)
     ap.add_argument("--restart-args", default="", help="arguments appended on restarts, e.g. \"--resume\"")
+    ap.add_argument("--restart-nproc", type=int, default=None, help="ranks for restarts (elastic; default: nproc)")
     ap.add_argument("nproc", type=int)
     ap.add_argument("argv", nargs=argparse.REMAINDER)
     a = ap.parse_args()
-    sys.exit(launch_with_restarts(a.nproc, a.argv, a.max_restarts, shlex.split(a.restart_args), a.timeout))
+    sys.exit(launch_with_restarts(a.nproc, a.argv, a.max_restarts, shlex.split(a.restart_args), a.timeout,
+                                  restart_nproc=a.restart_nproc))
 
 
 if __name__ == "__main__":

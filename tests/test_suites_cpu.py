@@ -213,3 +213,37 @@ def test_eval_matches_across_pipeline_layouts(tmp_path):
         assert len(evals) == 1, name
         out[name] = evals[0]
     assert abs(out["single"] - out["1f1b"]) < 1e-4 and abs(out["single"] - out["interleaved"]) < 1e-4, out
+
+
+def test_elastic_restart_on_fewer_ranks(tmp_path):
+    """tp2 x dp2 on 4 ranks; a rank fails at step 3; the job comes back on 2
+    ranks as tp1 x dp2 from the resharded step-2 checkpoint and finishes with
+    weights matching an uninterrupted tp2 run (fp32, up to rounding)."""
+    import torch
+
+    from dstraining_b200.models.gpt import GPT, GPTConfig
+    from dstraining_b200.parallel.topology import SINGLE
+    from dstraining_b200.utils import checkpoint
+    from dstraining_b200.utils.launch import launch_with_restarts
+
+    root = os.path.dirname(SUITES)
+    train = os.path.join(os.path.dirname(root), "train.py")
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="1")
+    common = ["--dp", "2", "--tp", "2", "--layers", "2", "--heads", "4", "--embd", "64", "--block", "32",
+              "--vocab", "256", "--batch", "4", "--steps", "6", "--ckpt-every", "2", "--device", "cpu"]
+    assert launch(4, [train, *common, "--ckpt-dir", str(tmp_path / "ref")], timeout=300, env=env) == 0
+    once = tmp_path / "injected"
+    fenv = dict(env, DST_INJECT_FAULT="1:3", DST_INJECT_FAULT_ONCE=str(once))
+    rc = launch_with_restarts(4, [train, *common, "--ckpt-dir", str(tmp_path / "ck")], max_restarts=1,
+                              restart_args=["--resume", "--tp", "1"], timeout=300, env=fenv, restart_nproc=2)
+    assert rc == 0 and once.exists()
+    info = checkpoint.inspect(str(tmp_path / "ck" / "step_00000006"))
+    assert info["ok"] and info["topology"]["tp"] == 1
+
+    def full(path):
+        m = GPT(GPTConfig(vocab_size=256, block_size=32, n_layer=2, n_head=4, n_embd=64), SINGLE, seed=0)
+        checkpoint.load(path, m, None, SINGLE)
+        return dict(m.named_parameters())
+
+    a, b = full(str(tmp_path / "ref" / "step_00000006")), full(str(tmp_path / "ck" / "step_00000006"))
+    assert max((a[k] - b[k]).abs().max().item() for k in a) < 1e-4
