@@ -24,6 +24,7 @@ import torch
 import torch.distributed as dist
 
 from .models.gpt import GPT, GPTChunks, GPTConfig, GPTStage
+from .optim.clip import clip_grad_norm
 from .optim.fused_dp import FusedDPAdam
 from .optim.precision import MasterWeightOptimizer
 from .optim.schedule import lr_at, set_lr
@@ -64,6 +65,8 @@ def add_args(p: argparse.ArgumentParser) -> argparse.ArgumentParser:
     p.add_argument("--lr-schedule", choices=["constant", "cosine"], default="constant")
     p.add_argument("--warmup-steps", type=int, default=0, help="linear learning-rate warm-up")
     p.add_argument("--min-lr", type=float, default=0.0, help="final rate of the cosine schedule")
+    p.add_argument("--grad-clip", type=float, default=0.0,
+                   help="clip the global gradient norm to this value (0: off; not with the fused DP optimizer)")
     p.add_argument("--seed", type=int, default=1337)
     p.add_argument("--log-every", type=int, default=1)
     p.add_argument("--device", default=None, help="cuda|cpu (default: cuda if available)")
@@ -167,6 +170,10 @@ class Trainer:
         else:
             # multi-tensor (foreach) Adam also on CPU, where PyTorch defaults to the per-tensor loop
             self.opt = torch.optim.Adam(model.parameters(), lr=args.lr, foreach=True)
+        if getattr(args, "grad_clip", 0.0) and self.fused_dp:
+            raise ValueError("--grad-clip needs the unfused optimizer path (the fused DP optimizer updates "
+                             "inside backward); set DST_FUSED_DP=0 or --naive-dp")
+        self.last_grad_norm = None
         self.reducer = None
         if self.dp.enabled and not args.naive_dp and not self.fused_dp:
             self.reducer = GradReducer(
@@ -226,6 +233,8 @@ class Trainer:
                 allreduce_gradients(self.model, self.dp)
         with nvtx_range("finalize_grads"):
             self.model.finalize_grads()
+        if getattr(a, "grad_clip", 0.0):
+            self.last_grad_norm = clip_grad_norm(self.model, a.grad_clip, self.tp, self.dp)
         with nvtx_range("optimizer"):
             self.opt.step()
         self.step_index += 1

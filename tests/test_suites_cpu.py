@@ -247,3 +247,27 @@ def test_elastic_restart_on_fewer_ranks(tmp_path):
 
     a, b = full(str(tmp_path / "ref" / "step_00000006")), full(str(tmp_path / "ck" / "step_00000006"))
     assert max((a[k] - b[k]).abs().max().item() for k in a) < 1e-4
+
+
+@pytest.mark.parametrize("n,args", [(2, ()), (2, ("--sp",)), (4, ("--sp",))])
+def test_grad_norm_suite(n, args):
+    run(n, "clip_suite.py", *args)
+
+
+def test_grad_clip_cli_same_norm_across_layouts(tmp_path):
+    """--grad-clip: the logged (pre-clip) global norm at step 0 is the same for
+    one rank and for pp2 x tp2 (and training runs with clipping active)."""
+    import json
+
+    root = os.path.dirname(SUITES)
+    train = os.path.join(os.path.dirname(root), "train.py")
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="1")
+    common = ["--layers", "4", "--heads", "4", "--embd", "64", "--block", "32", "--vocab", "256", "--batch", "4",
+              "--micro", "2", "--steps", "3", "--grad-clip", "0.5", "--device", "cpu"]
+    norms = {}
+    for name, n, extra in [("single", 1, []), ("pp2tp2", 4, ["--pp", "2", "--tp", "2", "--sp"])]:
+        sink = tmp_path / f"{name}.jsonl"
+        assert launch(n, [train, *common, *extra, "--jsonl", str(sink)], timeout=300, env=env) == 0, name
+        recs = [json.loads(ln) for ln in sink.read_text().splitlines()]
+        norms[name] = recs[0]["grad_norm"]
+    assert abs(norms["single"] - norms["pp2tp2"]) / norms["single"] < 1e-4, norms

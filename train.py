@@ -89,6 +89,8 @@ def run(args):
                 status = int(native.lib().read_status(False))
             ms_max, status_max = tr.world_max([ms, status])
             record = {"step_ms_max": round(ms_max, 3), "status": int(status_max)}
+            if tr.last_grad_norm is not None:
+                record["grad_norm"] = tr.last_grad_norm  # before clipping
             if cuda:
                 record["max_mem_gb"] = round(torch.cuda.max_memory_allocated(tr.device) / 2**30, 3)
         if tr.pp.is_last and logging:
