@@ -271,3 +271,26 @@ def test_grad_clip_cli_same_norm_across_layouts(tmp_path):
         recs = [json.loads(ln) for ln in sink.read_text().splitlines()]
         norms[name] = recs[0]["grad_norm"]
     assert abs(norms["single"] - norms["pp2tp2"]) / norms["single"] < 1e-4, norms
+
+
+def test_all_options_together(tmp_path):
+    """dp2 x tp2 + SP with accumulation, block recompute, clipping, a cosine
+    schedule, evaluation, background checkpoints, the step gate and heartbeats
+    in one job."""
+    import json
+
+    from dstraining_b200.utils import checkpoint
+
+    root = os.path.dirname(SUITES)
+    train = os.path.join(os.path.dirname(root), "train.py")
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="1")
+    sink = tmp_path / "m.jsonl"
+    argv = [train, "--dp", "2", "--tp", "2", "--sp", "--vp", "--recompute-blocks", "--grad-accum", "--micro", "2",
+            "--batch", "4", "--layers", "2", "--heads", "4", "--embd", "64", "--block", "32", "--vocab", "256",
+            "--steps", "6", "--grad-clip", "1.0", "--lr-schedule", "cosine", "--warmup-steps", "2",
+            "--eval-every", "3", "--ckpt-dir", str(tmp_path / "ck"), "--ckpt-every", "2", "--ckpt-async",
+            "--step-gate-timeout", "60", "--heartbeat-timeout", "120", "--jsonl", str(sink), "--device", "cpu"]
+    assert launch(4, argv, timeout=400, env=env) == 0
+    recs = [json.loads(ln) for ln in sink.read_text().splitlines()]
+    assert sum("eval_loss" in r for r in recs) == 2 and all("grad_norm" in r for r in recs if "loss" in r)
+    assert checkpoint.inspect(checkpoint.latest(str(tmp_path / "ck")))["ok"]
