@@ -108,6 +108,25 @@ CONFIGS = {
 }
 
 
+def model_flops_per_step(cfg: BenchConfig, lay: dict) -> float:
+    """Model FLOPs of one optimizer step (forward + backward = 3 x forward, no
+    recompute counted): linear layers 2 x 12 d^2 per token and layer, LM head
+    2 d V per token, causal attention 2 T d per token and layer."""
+    tokens = cfg.batch(lay) * cfg.block * lay["dp"]
+    d, L = cfg.embd, cfg.layers
+    fwd = tokens * (2 * 12 * d * d * L + 2 * d * cfg.vocab + 2 * cfg.block * d * L)
+    return 3.0 * fwd
+
+
+def measured_bf16_tflops() -> Optional[float]:
+    """Sustained bf16 GEMM throughput measured on this GPU type, if recorded."""
+    try:
+        with open(os.path.join(HERE, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops_sustained"])
+    except (OSError, KeyError, ValueError):
+        return None
+
+
 def parallelism_name(lay: dict) -> str:
     parts = [f"{k}{lay[k]}" for k in ("tp", "pp", "dp") if lay[k] > 1]
     if lay["chunks"] > 1:
@@ -469,6 +488,13 @@ def main():
             "ms_per_step": round(res["e2e_ms"], 3),
         },
     }
+    flops = model_flops_per_step(cfg, lay)
+    per_gpu = flops / (res["ms"] / 1000.0) / world / 1e12
+    out["model_tflop_per_step"] = round(flops / 1e12, 3)
+    out["achieved_tflops_per_gpu"] = round(per_gpu, 1)
+    peak = measured_bf16_tflops()
+    if peak:
+        out["fraction_of_measured_sustained_bf16"] = round(per_gpu / peak, 3)
     if res.get("note"):
         out["note"] = res["note"]
     if res["sampler"] is not None:

@@ -46,3 +46,14 @@ def test_baseline_layouts():
     lay5 = c["c5"].layout(8)
     assert lay5 == dict(tp=2, pp=2, dp=2, chunks=1) and c["c5"].batch(lay5) * lay5["dp"] == 64
     assert bench.parallelism_name(lay5) == "tp2xpp2xdp2"
+
+
+def test_model_flops():
+    bench = _bench()
+    c2 = bench.CONFIGS["c2"]
+    lay = c2.layout(1)
+    n, d, L, V, T = 16 * 1024, 768, 12, 50304, 1024
+    want = 3 * n * (24 * d * d * L + 2 * d * V + 2 * T * d * L)
+    assert bench.model_flops_per_step(c2, lay) == want
+    assert abs(want / 1e12 - 13.08) < 0.05  # GPT-2 small, 16 x 1024 tokens
+    assert bench.model_flops_per_step(c2, c2.layout(8)) == 8 * want  # weak scaling: 8 replicas
