@@ -27,7 +27,10 @@ optimizer state, activations), far more than the 126 MB L2, so no explicit
 L2 flush is needed. SM clocks and throttle reasons are sampled with
 nvidia-smi during the timed region. A second timed loop runs the same steps
 end to end through the public API (``Trainer.step``: pinned host batch ->
-device copy -> step -> loss read back), which is the ``e2e`` figure.
+device copy -> step -> loss read back), which is the ``e2e`` figure. The
+line also carries the model FLOPs per step (3 x forward, no recompute),
+the achieved TFLOP/s per GPU and, when ``MEASURED_PEAKS.json`` is present,
+the fraction of the measured sustained bf16 GEMM peak.
 
 ``--impl reference`` runs the unmodified reference package installed under
 ``baseline/_ref`` through its own public API (its GPT / GPTStage,
