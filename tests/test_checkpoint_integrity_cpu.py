@@ -34,3 +34,19 @@ def test_checksums_inspect_and_corruption(tmp_path, capsys):
     assert checkpoint.inspect(path)["corrupt"] == ["shard_tp0_pp0.pt"]
     with pytest.raises(RuntimeError, match="SHA-256"):
         checkpoint.load(path, _model(), None, SINGLE)
+
+
+def test_background_write_error_surfaces(tmp_path, monkeypatch):
+    """A failing background write is re-raised by wait() and leaves no
+    COMPLETE marker, so ``latest`` never picks the broken checkpoint."""
+    m = _model()
+
+    def broken_save(*a, **k):
+        raise OSError("disk full")
+
+    monkeypatch.setattr(checkpoint.torch, "save", broken_save)
+    pending = checkpoint.save(str(tmp_path), 9, m, None, SINGLE, PP_SINGLE, SINGLE, m.config, 3, background=True)
+    with pytest.raises(RuntimeError, match="failed") as e:
+        pending.wait()
+    assert isinstance(e.value.__cause__, OSError)
+    assert checkpoint.latest(str(tmp_path)) is None
