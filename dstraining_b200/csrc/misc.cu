@@ -42,7 +42,7 @@ __global__ void embed_fwd_kernel(const int64_t* __restrict__ idx, const __nv_bfl
   const int b = r / tl, t = t0 + r % tl;
   int64_t tok = idx[static_cast<size_t>(b) * T + t];
   if (tok < 0 || tok >= V) {
-    if (lane == 0) record_status(status, kBadArgument);
+    if (lane == 0) record_status(status, kIndexOutOfRange);
     tok = 0;
   }
   const uint4* e = reinterpret_cast<const uint4*>(wte + static_cast<size_t>(tok) * C);
@@ -75,16 +75,21 @@ __global__ void embed_bwd_pos_kernel(const __nv_bfloat16* __restrict__ dy, __nv_
 }
 
 // One warp per run of equal ids in the stably sorted token list: sums those
-// gradient rows in token order into wte's row.
+// gradient rows in token order into wte's row. An id outside [0, V) is
+// recorded in the status word and its rows are dropped (never written).
 __global__ void embed_bwd_tok_kernel(const int64_t* __restrict__ sorted, const int64_t* __restrict__ perm,
                                      const __nv_bfloat16* __restrict__ dy, __nv_bfloat16* __restrict__ dwte, int N,
-                                     int C) {
+                                     int C, int64_t V, int* status) {
   const int warps = blockDim.x >> 5;
   const int i = blockIdx.x * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (i >= N) return;
   const int64_t tok = sorted[i];
   if (i > 0 && sorted[i - 1] == tok) return;  // not the start of a run
+  if (tok < 0 || tok >= V) {
+    if (lane == 0) record_status(status, kIndexOutOfRange);
+    return;
+  }
   int end = i + 1;
   while (end < N && sorted[end] == tok) ++end;
   for (int v = lane; v < C / 8; v += 32) {
@@ -154,11 +159,15 @@ __global__ void adam_kernel(const __grid_constant__ AdamTable tab, float lr, flo
 
 // ---------------------------------------------------------------- fused CE
 // Merge per-(row, tile) softmax statistics in tile order -> per-row (max,
-// sum exp relative to max).
+// sum exp relative to max). A target id outside [0, vocab) (which no tile
+// can match) is recorded in the status word.
 __global__ void ce_merge_tiles_kernel(const float* __restrict__ tmax, const float* __restrict__ tsum, int M, int tiles,
-                                      float* __restrict__ row_max, float* __restrict__ row_sum) {
+                                      float* __restrict__ row_max, float* __restrict__ row_sum,
+                                      const int64_t* __restrict__ targets, int64_t vocab, int* status) {
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= M) return;
+  const int64_t tgt = targets[r];
+  if (tgt < 0 || tgt >= vocab) record_status(status, kIndexOutOfRange);
   float m = -INFINITY, s = 0.f;
   for (int t = 0; t < tiles; ++t) {
     const float tm = tmax[static_cast<size_t>(r) * tiles + t];
@@ -237,7 +246,8 @@ std::vector<at::Tensor> embedding_bwd(const at::Tensor& dy, const at::Tensor& id
   const int N = B * T, threads = 256, per = threads / 32;
   embed_bwd_tok_kernel<<<(N + per - 1) / per, threads, 0, st>>>(keys.data_ptr<int64_t>(), perm.data_ptr<int64_t>(),
                                                                 reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()),
-                                                                reinterpret_cast<__nv_bfloat16*>(dwte.data_ptr()), N, C);
+                                                                reinterpret_cast<__nv_bfloat16*>(dwte.data_ptr()), N, C,
+                                                                vocab, status_ptr());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {dwte, dwpe};
 }
@@ -287,15 +297,22 @@ void adam_master_step(const std::vector<at::Tensor>& params, const std::vector<a
   }
 }
 
-std::vector<at::Tensor> ce_merge_tiles(const at::Tensor& tmax, const at::Tensor& tsum) {
+// targets: the [rows] int64 target ids (checked against the real vocabulary
+// size, not used otherwise).
+std::vector<at::Tensor> ce_merge_tiles(const at::Tensor& tmax, const at::Tensor& tsum, const at::Tensor& targets,
+                                       int64_t vocab) {
   TORCH_CHECK(tmax.scalar_type() == at::kFloat && tmax.is_contiguous() && tsum.sizes() == tmax.sizes(), "ce_merge");
   TORCH_CHECK(tmax.is_cuda() && tmax.dim() == 2 && tsum.is_contiguous(), "ce_merge: [rows, tiles] fp32 statistics");
-  c10::cuda::CUDAGuard g(tmax.device());
   const int M = tmax.size(0), tiles = tmax.size(1);
+  TORCH_CHECK(targets.is_cuda() && targets.scalar_type() == at::kLong && targets.is_contiguous() &&
+                  targets.numel() == M && vocab > 0,
+              "ce_merge: one contiguous int64 target per row and vocab > 0");
+  c10::cuda::CUDAGuard g(tmax.device());
   at::Tensor m = at::empty({M}, tmax.options());
   at::Tensor s = at::empty({M}, tmax.options());
   ce_merge_tiles_kernel<<<(M + 255) / 256, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      tmax.data_ptr<float>(), tsum.data_ptr<float>(), M, tiles, m.data_ptr<float>(), s.data_ptr<float>());
+      tmax.data_ptr<float>(), tsum.data_ptr<float>(), M, tiles, m.data_ptr<float>(), s.data_ptr<float>(),
+      targets.data_ptr<int64_t>(), vocab, status_ptr());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {m, s};
 }

@@ -32,6 +32,7 @@ enum StatusCode : int {
   kTimeoutTmemEmpty = 4,
   kTimeoutPeer = 5,
   kBadArgument = 6,
+  kIndexOutOfRange = 7,  // a token or target id outside the vocabulary
 };
 
 // 2 s: far above any legitimate wait inside one kernel on this hardware.

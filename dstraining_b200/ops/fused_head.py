@@ -50,7 +50,7 @@ class _FusedHeadCE(torch.autograd.Function):
                 x = all_gather_dim(x, tp, 1)
             x2 = x.reshape(-1, x.shape[-1]).contiguous()
             logits, tmax, tsum, tgt = lib.gemm_ce_stats(x2, w, tg, col0, valid)
-        m, s = lib.ce_merge_tiles(tmax, tsum)
+        m, s = lib.ce_merge_tiles(tmax, tsum, tg, real_vocab)  # also flags target ids outside the vocabulary
         stats = torch.stack([m, s, tgt])[None]
         if tp.enabled:
             stats = all_gather_dim(stats, tp, 0)

@@ -34,6 +34,7 @@ STATUS_NAMES = {
     4: "timeout waiting for a free TMEM accumulator",
     5: "timeout waiting for a peer rank",
     6: "bad argument",
+    7: "token or target id outside the vocabulary",
 }
 
 

@@ -22,6 +22,7 @@ Takes ``train.py``'s flags and reports, without building the model:
 
 from __future__ import annotations
 
+import argparse
 import json
 import sys
 from typing import Dict, List, Optional
@@ -47,6 +48,9 @@ def stage_params(args, stage: int, tp: int) -> int:
 
 
 def plan(args) -> Dict:
+    if getattr(args, "gpt2", False):  # the preset the trainer applies (GPT-2 124M shape)
+        args = argparse.Namespace(**{**vars(args), "layers": 12, "heads": 12, "embd": 768, "block": 1024,
+                                     "vocab": 50257})
     tp, pp, dp, v = args.tp, args.pp, args.dp, args.chunks
     errors: List[str] = []
     warnings: List[str] = []

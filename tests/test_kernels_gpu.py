@@ -133,6 +133,35 @@ def test_embedding():
     assert dwpe[T:].abs().max().item() == 0
 
 
+def test_ids_outside_vocabulary_are_reported():
+    """A token id or a target id outside the vocabulary is recorded in the
+    status word (code 7); the embedding backward drops its rows instead of
+    writing outside the table."""
+    lib = _lib()
+    V, P, C, B, T = 1000, 128, 256, 2, 128
+    wte, wpe = _bf(V, C, seed=19), _bf(P, C, seed=20)
+    idx = torch.randint(0, V, (B, T), device="cuda")
+    idx[1, 5] = V + 3
+    lib.embedding_fwd(idx, wte, wpe, 0, T)
+    torch.cuda.synchronize()
+    assert lib.read_status(True) == 7
+    dy = _bf(B, T, C, seed=21)
+    dwte, _ = lib.embedding_bwd(dy, idx, V, P)
+    torch.cuda.synchronize()
+    assert lib.read_status(True) == 7
+    keep = (idx != V + 3).reshape(-1)
+    rwte = torch.zeros(V, C, device="cuda").index_add_(0, idx.reshape(-1)[keep], dy.float().reshape(-1, C)[keep])
+    assert _rel(dwte, rwte) < 1e-2
+    tmax = torch.zeros(4, 3, device="cuda")
+    tsum = torch.ones(4, 3, device="cuda")
+    lib.ce_merge_tiles(tmax, tsum, torch.tensor([0, 5, 9, 2], device="cuda"), 10)
+    torch.cuda.synchronize()
+    assert lib.read_status(True) == 0
+    lib.ce_merge_tiles(tmax, tsum, torch.tensor([0, 5, 10, 2], device="cuda"), 10)
+    torch.cuda.synchronize()
+    assert lib.read_status(True) == 7
+
+
 def _ref_attention(qkv, H, D):
     B, T, _ = qkv.shape
     y = qkv.float().view(B, T, H, 3, D)

@@ -42,3 +42,11 @@ def test_reports_invalid_and_slow_layouts(capsys):
     with pytest.raises(SystemExit) as e:
         main([*BASE, "--tp", "2"])
     assert e.value.code == 0 and '"valid": true' in capsys.readouterr().out
+
+
+def test_gpt2_preset():
+    # GPT-2 124M shape with an untied head over the padded vocabulary: 163,073,280 parameters
+    out = plan(parse_args(["--gpt2", "--bf16", "--vp", "--batch", "16"]))
+    assert out["valid"] and out["per_stage"][0]["params"] == 50257 * 768 + 1024 * 768 + 12 * (12 * 768 * 768 + 13 * 768) \
+        + 2 * 768 + 50304 * 768
+    assert out["tokens_per_step"] == 16 * 1024
