@@ -19,10 +19,12 @@ bitwise identical across the group. The reference issues three all-reduces
 stats needs one collective and is the same algebra as a flash-attention
 softmax merge.
 
-Padded vocab columns (global id >= ``real_vocab``) are masked to -inf: they
-add nothing to the denominator and get zero gradient. Backward is local:
-``(softmax - onehot) * grad / N`` on this rank's columns, recomputed from the
-saved logits and the per-row ``lse`` instead of saving an fp32 ``exp`` copy.
+Padded vocab columns (global id >= ``real_vocab``) are masked out: they add
+nothing to the denominator and get zero gradient. Backward is local:
+``(softmax - onehot) * grad / N`` on this rank's columns. Forward keeps the
+shard's ``exp(l - m)`` (it needs it for the sum anyway, and it takes the
+place of the fp32 logits), so backward is one per-row rescale by
+``exp(m - lse) * grad / N`` - no second exponential pass over ``[N, V]``.
 
 This module is the PyTorch path (CPU, fp32 oracle). On CUDA bf16 the head
 GEMM and this reduction are fused into one native kernel
@@ -37,20 +39,6 @@ from ..parallel.comm import all_gather_dim
 from ..parallel.topology import TPContext
 
 
-def shard_stats(lf: torch.Tensor, targets: torch.Tensor, vocab_start: int):
-    """Per-row (max, sumexp relative to max, target logit) of one vocab shard.
-    ``lf`` is fp32 with padded columns already at -inf."""
-    n, v_local = lf.shape
-    m = lf.max(dim=1).values
-    m_safe = torch.where(torch.isinf(m), torch.zeros_like(m), m)
-    s = torch.exp(lf - m_safe[:, None]).sum(dim=1)
-    local_t = targets - vocab_start
-    in_range = (local_t >= 0) & (local_t < v_local)
-    picked = lf.gather(1, local_t.clamp(0, v_local - 1)[:, None]).squeeze(1)
-    t = torch.where(in_range, picked, torch.zeros_like(picked))
-    return m_safe, s, t, in_range
-
-
 def merge_stats(stats: torch.Tensor) -> torch.Tensor:
     """stats: [R, 3, N] rows (m, s, t) from R shards -> (lse [N], target [N])."""
     m, s, t = stats[:, 0], stats[:, 1], stats[:, 2]
@@ -63,30 +51,45 @@ class _VocabParallelCE(torch.autograd.Function):
     @staticmethod
     def forward(ctx, logits, targets, tp, vocab_start, real_vocab):
         in_dtype = logits.dtype
-        lf = logits.float().clone()
-        real_cols = real_vocab - vocab_start
-        if real_cols < lf.shape[1]:
-            lf[:, max(real_cols, 0):] = float("-inf")
-        m, s, t, in_range = shard_stats(lf, targets, vocab_start)
-        stats = torch.stack([m, s, t])[None]  # [1, 3, N]
+        lf = logits.float()
+        n, v_local = lf.shape
+        real_cols = min(max(real_vocab - vocab_start, 0), v_local)
+        # per-row max over the real columns (-inf for a shard of padding only)
+        if real_cols > 0:
+            m = lf[:, :real_cols].max(dim=1).values
+        else:
+            m = torch.full((n,), float("-inf"), dtype=lf.dtype, device=lf.device)
+        m_safe = torch.where(torch.isinf(m), torch.zeros_like(m), m)
+        e = torch.sub(lf, m_safe[:, None])
+        e.exp_()
+        if real_cols < v_local:
+            e[:, real_cols:] = 0.0
+        s = e.sum(dim=1)
+        local_t = targets - vocab_start
+        in_range = (local_t >= 0) & (local_t < v_local)
+        picked = lf.gather(1, local_t.clamp(0, v_local - 1)[:, None]).squeeze(1)
+        # a target on a padded column reads as -inf (an infinite loss), as if masked
+        picked = torch.where(local_t >= real_cols, torch.full_like(picked, float("-inf")), picked)
+        t = torch.where(in_range, picked, torch.zeros_like(picked))
+        stats = torch.stack([m_safe, s, t])[None]  # [1, 3, N]
         if tp.enabled:
             stats = all_gather_dim(stats, tp, 0)
         lse, tgt = merge_stats(stats)
         loss = (lse - tgt).mean()
-        ctx.save_for_backward(lf, lse, targets, in_range)
+        ctx.save_for_backward(e, m_safe, lse, targets, in_range)
         ctx.vocab_start = vocab_start
         ctx.in_dtype = in_dtype
         return loss
 
     @staticmethod
     def backward(ctx, grad):
-        lf, lse, targets, in_range = ctx.saved_tensors
-        n, v_local = lf.shape
-        p = torch.exp(lf - lse[:, None])
-        rows = torch.arange(n, device=lf.device)
+        e, m, lse, targets, in_range = ctx.saved_tensors
+        n, v_local = e.shape
+        scale = grad / n
+        p = e * (torch.exp(m - lse) * scale)[:, None]  # softmax * grad / N
+        rows = torch.arange(n, device=e.device)
         cols = (targets - ctx.vocab_start).clamp(0, v_local - 1)
-        p[rows, cols] -= in_range.to(p.dtype)
-        p *= grad / n
+        p[rows, cols] -= in_range.to(p.dtype) * scale
         return p.to(ctx.in_dtype), None, None, None, None
 
 

@@ -339,8 +339,10 @@ def load(path: str, model: nn.Module, opt, tp) -> dict:
             elif isinstance(opt, torch.optim.Optimizer):
                 ea, eas = local(f"exp_avg/{g}", name, p), local(f"exp_avg_sq/{g}", name, p)
                 if ea is not None and eas is not None:
+                    fused = bool(opt.defaults.get("fused"))  # fused Adam keeps its step on the params' device
                     opt.state[p] = {
-                        "step": torch.tensor(opt_step),
+                        "step": torch.tensor(float(opt_step), dtype=torch.float32,
+                                             device=p.device if fused else "cpu"),
                         "exp_avg": ea.to(p.device, p.dtype).clone(),
                         "exp_avg_sq": eas.to(p.device, p.dtype).clone(),
                     }
