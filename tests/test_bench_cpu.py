@@ -57,3 +57,31 @@ def test_model_flops():
     assert bench.model_flops_per_step(c2, lay) == want
     assert abs(want / 1e12 - 13.08) < 0.05  # GPT-2 small, 16 x 1024 tokens
     assert bench.model_flops_per_step(c2, c2.layout(8)) == 8 * want  # weak scaling: 8 replicas
+
+
+@pytest.mark.parametrize("impl", ["ours", "reference"])
+def test_json_line(impl, monkeypatch, capsys):
+    """main() turns one arm's measurements into the one JSON line the driver
+    reads (arm faked: no GPU here), with every required key."""
+    import json
+
+    bench = _bench()
+    for k, v in dict(RANK="0", WORLD_SIZE="1", LOCAL_RANK="0").items():
+        monkeypatch.setenv(k, v)
+    fake = dict(ms=22.6, e2e_ms=23.0, loss=10.9, launches=(452, 50, [("x", 1)]), h2d=262144, d2h=4, sampler=None,
+                status=0, n_params=163_073_280, note=None if impl == "ours" else "stock code path")
+    monkeypatch.setattr(bench, "run_ours", lambda *a, **k: fake)
+    monkeypatch.setattr(bench, "run_reference", lambda *a, **k: fake)
+    monkeypatch.setattr(sys, "argv", ["bench.py", "--impl", impl, "--steps", "5", "--warmup", "3"])
+    bench.main()
+    line = capsys.readouterr().out.strip().splitlines()[-1]
+    out = json.loads(line)
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better", "scaling",
+                "vs_baseline", "dtype", "data", "config", "e2e", "gpu_launches", "impl"):
+        assert key in out, key
+    assert out["n_gpus"] == 1 and out["steps"] == 5 and out["warmup"] == 3 and out["impl"] == impl
+    assert abs(out["value"] - 16 * 1024 / 0.0226) < 1 and out["higher_is_better"] is True
+    assert out["config"]["global_batch"] == 16 and out["config"]["seq_len"] == 1024
+    assert set(out["e2e"]) >= {"value", "unit", "h2d_bytes_per_step", "d2h_bytes_per_step"}
+    assert out["gpu_launches"] == (452 * 5 if impl == "ours" else None)
+    assert out["model_tflop_per_step"] > 13
