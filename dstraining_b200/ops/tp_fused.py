@@ -32,7 +32,7 @@ from typing import Dict, Optional, Tuple
 import torch
 
 from ..parallel.symm import PeerBuffer
-from ..parallel.topology import TPContext
+from ..parallel.topology import TPContext, peer_reachable
 from . import native
 from .gemm import EPI_BIAS, EPI_BIAS_GELU, EPI_DGELU, EPI_STORE, bias_grad, gemm, weight_grad
 
@@ -259,5 +259,8 @@ def mlp_sequence_parallel(x, w1, b1, w2, b2, residual, tp):
 
 
 def usable(tp: TPContext, seq: int) -> bool:
-    """The fused kernels need sequence shards of a multiple of 128 tokens."""
-    return tp.enabled and tp.world <= 8 and seq % tp.world == 0 and (seq // tp.world) % 128 == 0
+    """The fused kernels need sequence shards of a multiple of 128 tokens and
+    a group whose ranks can address each other's GPU memory (one host; the
+    first call per group is a collective, see ``peer_reachable``)."""
+    return (tp.enabled and tp.world <= 8 and seq % tp.world == 0 and (seq // tp.world) % 128 == 0
+            and peer_reachable(tp))

@@ -37,7 +37,7 @@ import torch.distributed as dist
 
 from ..ops import native
 from ..parallel.dp import build_buckets
-from ..parallel.topology import DPContext
+from ..parallel.topology import DPContext, peer_reachable
 
 _ALIGN = 8  # elements per rank slice are a multiple of this (16-byte vectors)
 
@@ -113,6 +113,9 @@ class FusedDPAdam:
         self.native = p0.is_cuda and native.enabled()
         if self.native and (self.dtype != torch.bfloat16 or dp.world > 8):
             raise ValueError("fused DP Adam on CUDA needs bf16 parameters and at most 8 ranks")
+        if self.native and not peer_reachable(dp):
+            raise ValueError("fused DP Adam on CUDA needs every DP rank on this host with a GPU it can address "
+                             "(CUDA IPC); use GradReducer + MasterWeightOptimizer across machines")
         order = self.model_params[::-1]
         late = [p for p in order if getattr(p, "sequence_parallel_replicated", False)]
         early = [p for p in order if not getattr(p, "sequence_parallel_replicated", False)]

@@ -203,3 +203,78 @@ def make_topology(tp_size: int = 1, pp_size: int = 1, dp_size: int = 1):
                 dp = DPContext(group=pg, rank=dp_rank, world=dp_size, ranks=members)
     assert dp is not None
     return tp, pp, dp
+
+
+# ---------------------------------------------------------------- peer memory
+_PEER_OK = {}  # group ranks -> bool
+
+
+def _host_id() -> str:
+    """This machine: host name plus the kernel's boot id (host names alone can
+    repeat across containers on different machines)."""
+    import socket
+
+    boot = ""
+    try:
+        with open("/proc/sys/kernel/random/boot_id") as f:
+            boot = f.read().strip()
+    except OSError:
+        pass
+    return f"{socket.gethostname()}/{boot}"
+
+
+def _pci_id(index: int) -> str:
+    p = torch.cuda.get_device_properties(index)
+    return f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}"
+
+
+def peers_addressable(infos, me: int, visible, can_access) -> bool:
+    """Decision behind :func:`peer_reachable`, on the gathered facts.
+
+    ``infos[r]`` is rank r's ``(host id, PCI id of its GPU)``; ``visible``
+    maps the PCI ids of the GPUs this process can see to their device
+    indices; ``can_access(a, b)`` answers whether device a can address
+    device b's memory directly. True when every rank runs on this host, on a
+    distinct GPU that this process sees and can address."""
+    host, pci = infos[me]
+    if pci not in visible or len({i[1] for i in infos}) != len(infos):
+        return False
+    mine = visible[pci]
+    for r, (h, p) in enumerate(infos):
+        if r == me:
+            continue
+        if h != host or p not in visible or not can_access(mine, visible[p]):
+            return False
+    return True
+
+
+def peer_reachable(ctx: TPContext) -> bool:
+    """Whether the peer-memory kernels (the fused DP optimizer and the fused
+    tensor-parallel GEMMs, which load and store other ranks' buffers through
+    CUDA IPC mappings) can serve this group: every rank on this host, on a GPU
+    that this process can address directly. Groups spanning machines, or
+    processes that cannot see their peers' GPUs, use the NCCL paths instead.
+    ``DST_PEER=0`` forces the NCCL paths.
+
+    Collective over the group on the first call for a group (every member
+    must make it at the same point); cached afterwards. Single-rank groups
+    are trivially reachable."""
+    if not ctx.enabled:
+        return True
+    key = tuple(ctx.ranks)
+    if key in _PEER_OK:
+        return _PEER_OK[key]
+    ok = torch.cuda.is_available() and dist.is_initialized() and os.environ.get("DST_PEER", "1") != "0"
+    if torch.cuda.is_available() and dist.is_initialized():
+        # every member takes part in both gathers, whatever its own answer, and
+        # the group uses peer memory only if every member can: all agree
+        mine = (_host_id(), _pci_id(torch.cuda.current_device()))
+        infos = [None] * ctx.world
+        dist.all_gather_object(infos, mine, group=ctx.group)
+        visible = {_pci_id(i): i for i in range(torch.cuda.device_count())}
+        ok = ok and peers_addressable(infos, ctx.rank, visible, torch.cuda.can_device_access_peer)
+        votes = [None] * ctx.world
+        dist.all_gather_object(votes, bool(ok), group=ctx.group)
+        ok = all(votes)
+    _PEER_OK[key] = bool(ok)
+    return _PEER_OK[key]
