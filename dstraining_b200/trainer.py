@@ -74,6 +74,8 @@ def add_args(p: argparse.ArgumentParser) -> argparse.ArgumentParser:
     p.add_argument("--ckpt-dir", default=None, help="directory for sharded checkpoints")
     p.add_argument("--ckpt-every", type=int, default=0, help="save every N steps (0: only at the end if --ckpt-dir)")
     p.add_argument("--resume", action="store_true", help="resume from the latest checkpoint in --ckpt-dir")
+    p.add_argument("--ckpt-keep", type=int, default=0,
+                   help="keep only the newest N complete checkpoints (0: keep all)")
     p.add_argument("--ckpt-async", action="store_true",
                    help="write periodic checkpoints from a background thread (training continues)")
     p.add_argument("--jsonl", default=None, help="append per-step metrics (JSON lines) to this file")
@@ -153,9 +155,16 @@ class Trainer:
             self.pipe = Pipeline1F1B(model, self.pp, micro_batch_size=args.micro, seq_len=cfg.block_size)
         else:
             self.pipe = None
+        cuda = self.device.type == "cuda"
+        if cuda:
+            # whether each group's ranks can address each other's GPU memory (one
+            # host): collectives, made here by every rank in the same order, so
+            # the answer is cached before any forward pass asks for it
+            topology.peer_reachable(self.tp)
+            topology.peer_reachable(self.dp)
         self.fused_dp = (
-            args.bf16 and not args.naive_dp and self.device.type == "cuda"
-            and os.environ.get("DST_FUSED_DP", "1") != "0"
+            args.bf16 and not args.naive_dp and cuda and os.environ.get("DST_FUSED_DP", "1") != "0"
+            and self.dp.world <= 8 and topology.peer_reachable(self.dp)
         )
         if self.fused_dp:
             # DP reduction + fp32-master Adam + parameter all-gather in one

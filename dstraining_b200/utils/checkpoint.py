@@ -33,8 +33,9 @@ import datetime
 import hashlib
 import json
 import os
+import shutil
 import threading
-from typing import Dict, Optional
+from typing import Dict, List, Optional
 
 import torch
 import torch.distributed as dist
@@ -246,6 +247,27 @@ def save(root: str, step: int, model: nn.Module, opt, tp, pp, dp, config, seed: 
     handle._thread = t
     t.start()
     return handle
+
+
+def prune(root: str, keep: int) -> List[str]:
+    """Delete all but the newest ``keep`` COMPLETE checkpoints under ``root``,
+    and incomplete directories older than the newest complete one (writes
+    that failed). Directories newer than it are left alone: a background
+    write may still be filling one. Call from one process (rank 0) after a
+    checkpoint is complete; returns the deleted paths."""
+    if keep < 1 or not os.path.isdir(root):
+        return []
+    dirs = sorted(d for d in os.listdir(root) if d.startswith("step_") and os.path.isdir(os.path.join(root, d)))
+    complete = [d for d in dirs if os.path.exists(os.path.join(root, d, "COMPLETE"))]
+    if not complete:
+        return []
+    newest = complete[-1]
+    doomed = complete[:-keep] + [d for d in dirs if d < newest and d not in complete]
+    removed = []
+    for d in sorted(doomed):
+        shutil.rmtree(os.path.join(root, d), ignore_errors=True)
+        removed.append(os.path.join(root, d))
+    return removed
 
 
 def latest(root: str) -> Optional[str]:

@@ -8,7 +8,7 @@ parallelism, selective recompute and bf16 + fp32 master weights.
     torchrun --nproc_per_node 8 train.py --dp 8 --bf16 --vp --gpt2 --batch 16 --vocab 50304
 
 Same flags as the reference's ``train.py:29-58`` (plus ``--bucket-mb``,
-checkpointing, ``--heartbeat-timeout`` and ``--jsonl``, whose records carry
+checkpointing with retention, ``--heartbeat-timeout`` and ``--jsonl``, whose records carry
 the loss, tok/s, the device step time max over ranks, the peak memory and
 the kernels' status word). Logs ``step N  loss X  T tok/s`` from the
 last pipeline stage's tp0/dp0 rank; the loss is averaged over DP and the
@@ -39,6 +39,13 @@ def main():
 
             report_failure(f"{type(e).__name__}: {e}")
         raise
+
+
+def prune(args) -> None:
+    """Checkpoint retention (``--ckpt-keep``), by global rank 0 once a
+    checkpoint is complete."""
+    if args.ckpt_keep and (not dist.is_initialized() or dist.get_rank() == 0):
+        checkpoint.prune(args.ckpt_dir, args.ckpt_keep)
 
 
 def run(args):
@@ -114,13 +121,17 @@ def run(args):
         if args.ckpt_dir and args.ckpt_every and (step + 1) % args.ckpt_every == 0 and not last:
             if pending is not None:
                 pending.wait()  # one background write at a time
+                prune(args)
             out = checkpoint.save(args.ckpt_dir, step + 1, tr.model, tr.opt, tr.tp, tr.pp, tr.dp, tr.config,
                                   args.seed, background=args.ckpt_async)
             pending = out if args.ckpt_async else None
+            if pending is None:
+                prune(args)
     if pending is not None:
         pending.wait()
     if args.ckpt_dir:
         checkpoint.save(args.ckpt_dir, args.steps, tr.model, tr.opt, tr.tp, tr.pp, tr.dp, tr.config, args.seed)
+        prune(args)
     if sink:
         sink.close()
     if dist.is_initialized():
