@@ -3,16 +3,26 @@
     python -m dstraining_b200.utils.generate --ckpt ckpt/ --text "hello" --tokenizer bytes \
         --max-new-tokens 64 [--temperature 0.8 --top-k 40 --seed 0]
 
-``generate(model, idx, ...)`` extends ``idx`` [B, T] token by token with the
-full-context forward pass (no KV cache): the last ``block_size`` tokens are
-the context, right-padded to a multiple of ``pad_to`` so the native causal
-attention kernels (which take sequence lengths in multiples of 64 / 128) can
-run it - under causal attention the padding never influences the positions
-before it. ``temperature == 0`` is greedy decoding. Works for ``GPT`` at any
-tensor-parallel degree (every TP rank must call it with the same inputs and
-generator state); pipeline stages are not supported. The CLI loads a sharded
-checkpoint (any layout) into a single-process model. The reference has no
-sampling code.
+``generate(model, idx, ...)`` extends ``idx`` [B, T] token by token.
+``temperature == 0`` is greedy decoding.
+
+* With ``use_cache=True`` (the default; single-process models) the prompt is
+  run once and every later token costs one row per layer: its key and value
+  are appended to a per-layer cache and its query attends over the cache.
+  Positions are learned and absolute, so once the sequence outgrows
+  ``block_size`` the window slides and every step re-runs the whole window,
+  exactly as without a cache. Runs on the model's own parameters with
+  PyTorch ops (fp32 on CPU, the model's dtype on CUDA).
+* Otherwise (and for tensor-parallel models) every step runs the model's
+  full-context forward pass on the last ``block_size`` tokens, right-padded
+  to a multiple of ``pad_to`` so the native causal attention kernels (which
+  take sequence lengths in multiples of 64 / 128) can run it - under causal
+  attention the padding never influences the positions before it. Every TP
+  rank must call it with the same inputs and generator state; pipeline
+  stages are not supported.
+
+The CLI loads a sharded checkpoint (any layout) into a single-process model.
+The reference has no sampling code.
 """
 
 from __future__ import annotations
@@ -23,35 +33,101 @@ import os
 from typing import Optional
 
 import torch
+import torch.nn.functional as F
 
 from ..models.gpt import GPT, GPTConfig
 from ..parallel.topology import SINGLE
 
 
+class KVCache:
+    """Keys and values of every layer for the tokens seen so far, in
+    preallocated ``[B, H, block_size, D]`` buffers, and the decoding step of
+    a single-process :class:`GPT` over them (PyTorch ops on the model's
+    parameters)."""
+
+    def __init__(self, model: GPT, batch: int):
+        cfg = model.config
+        self.model = model
+        p = model.wte.weight
+        self.H, self.D = cfg.n_head, cfg.n_embd // cfg.n_head
+        shape = (batch, self.H, cfg.block_size, self.D)
+        self.k = [torch.empty(shape, dtype=p.dtype, device=p.device) for _ in range(cfg.n_layer)]
+        self.v = [torch.empty(shape, dtype=p.dtype, device=p.device) for _ in range(cfg.n_layer)]
+        self.len = 0
+
+    @staticmethod
+    def _ln(ln, x):
+        return F.layer_norm(x, ln.normalized_shape, ln.weight, ln.bias, ln.eps)
+
+    def forward(self, tokens: torch.Tensor) -> torch.Tensor:
+        """Run ``tokens`` [B, t] at positions ``len .. len + t - 1`` (the whole
+        window when the cache is empty, else one token), append their keys and
+        values, and return the logits [B, vocab] of the last one."""
+        m, cfg = self.model, self.model.config
+        b, t = tokens.shape
+        p0 = self.len
+        if p0 + t > cfg.block_size or (p0 > 0 and t != 1):
+            raise ValueError("KVCache.forward: a full window first, then one token at a time")
+        pos = torch.arange(p0, p0 + t, device=tokens.device)
+        x = F.embedding(tokens, m.wte.weight) + F.embedding(pos, m.wpe.weight)[None]
+        for i, blk in enumerate(m.blocks):
+            a = blk.attn
+            qkv = F.linear(self._ln(blk.ln_1, x), a.qkv.weight, a.qkv.bias).view(b, t, self.H, 3, self.D)
+            q, k, v = (qkv[:, :, :, j].transpose(1, 2) for j in range(3))
+            self.k[i][:, :, p0 : p0 + t] = k
+            self.v[i][:, :, p0 : p0 + t] = v
+            keys, vals = self.k[i][:, :, : p0 + t], self.v[i][:, :, : p0 + t]
+            # the window's first pass is causal; a single new token sees every cached one
+            y = F.scaled_dot_product_attention(q, keys, vals, is_causal=p0 == 0 and t > 1)
+            y = y.transpose(1, 2).reshape(b, t, cfg.n_embd)
+            x = x + F.linear(y, a.proj.weight, a.proj.bias)
+            h = F.gelu(F.linear(self._ln(blk.ln_2, x), blk.mlp.c_fc.weight, blk.mlp.c_fc.bias), approximate="tanh")
+            x = x + F.linear(h, blk.mlp.c_proj.weight, blk.mlp.c_proj.bias)
+        self.len = p0 + t
+        x = self._ln(m.ln_f, x[:, -1])
+        return F.linear(x, m.lm_head.weight)[:, : cfg.vocab_size]
+
+
+def _sample(logits: torch.Tensor, temperature: float, top_k: Optional[int], generator) -> torch.Tensor:
+    logits = logits.float()
+    if temperature <= 0:
+        return logits.argmax(dim=-1, keepdim=True)
+    logits = logits / temperature
+    if top_k is not None and top_k < logits.shape[-1]:
+        kth = torch.topk(logits, top_k, dim=-1).values[:, -1:]
+        logits = logits.masked_fill(logits < kth, float("-inf"))
+    probs = torch.softmax(logits, dim=-1)
+    return torch.multinomial(probs.cpu(), 1, generator=generator).to(logits.device)
+
+
+def _full_context_logits(model: GPT, idx: torch.Tensor, pad_to: int) -> torch.Tensor:
+    cfg = model.config
+    ctx = idx[:, -cfg.block_size:]
+    n = ctx.shape[1]
+    padded = min(cfg.block_size, -(-n // pad_to) * pad_to) if pad_to > 1 else n
+    if padded > n:
+        ctx = torch.cat([ctx, ctx.new_zeros(ctx.shape[0], padded - n)], dim=1)
+    logits, _ = model(ctx)
+    return logits[:, n - 1, : cfg.vocab_size]
+
+
 @torch.no_grad()
 def generate(model: GPT, idx: torch.Tensor, max_new_tokens: int, temperature: float = 1.0,
-             top_k: Optional[int] = None, generator: Optional[torch.Generator] = None, pad_to: int = 128) -> torch.Tensor:
+             top_k: Optional[int] = None, generator: Optional[torch.Generator] = None, pad_to: int = 128,
+             use_cache: bool = True) -> torch.Tensor:
     cfg = model.config
+    cache = KVCache(model, idx.shape[0]) if (use_cache and not model.tp.enabled) else None
     was_training = model.training
     model.eval()
     try:
         for _ in range(max_new_tokens):
-            ctx = idx[:, -cfg.block_size:]
-            n = ctx.shape[1]
-            padded = min(cfg.block_size, -(-n // pad_to) * pad_to) if pad_to > 1 else n
-            if padded > n:
-                ctx = torch.cat([ctx, ctx.new_zeros(ctx.shape[0], padded - n)], dim=1)
-            logits, _ = model(ctx)
-            logits = logits[:, n - 1, : cfg.vocab_size].float()
-            if temperature <= 0:
-                nxt = logits.argmax(dim=-1, keepdim=True)
+            if cache is None or idx.shape[1] > cfg.block_size:
+                logits = _full_context_logits(model, idx, pad_to)  # window slides: positions shift
+            elif cache.len == 0:
+                logits = cache.forward(idx)
             else:
-                logits = logits / temperature
-                if top_k is not None and top_k < logits.shape[-1]:
-                    kth = torch.topk(logits, top_k, dim=-1).values[:, -1:]
-                    logits = logits.masked_fill(logits < kth, float("-inf"))
-                probs = torch.softmax(logits, dim=-1)
-                nxt = torch.multinomial(probs.cpu(), 1, generator=generator).to(idx.device)
+                logits = cache.forward(idx[:, -1:])
+            nxt = _sample(logits, temperature, top_k, generator)
             idx = torch.cat([idx, nxt.to(idx.dtype)], dim=1)
     finally:
         model.train(was_training)

@@ -1,6 +1,7 @@
 """Sampling: right-padding the context (for the native attention kernels)
-does not change greedy outputs; the CLI samples from a sharded checkpoint
-written at tp=2."""
+does not change greedy outputs; the KV-cache decoder gives the full-context
+forward pass's logits and tokens (also once the window slides); the CLI
+samples from a sharded checkpoint written at tp=2."""
 
 import os
 
@@ -8,7 +9,7 @@ import torch
 
 from dstraining_b200.models.gpt import GPT, GPTConfig
 from dstraining_b200.parallel.topology import SINGLE
-from dstraining_b200.utils.generate import generate, main
+from dstraining_b200.utils.generate import KVCache, generate, main
 from dstraining_b200.utils.launch import launch
 
 
@@ -16,8 +17,8 @@ def test_padding_does_not_change_greedy_output():
     cfg = GPTConfig(vocab_size=300, block_size=64, n_layer=2, n_head=4, n_embd=64)
     m = GPT(cfg, SINGLE, seed=5)
     idx = torch.randint(0, 300, (2, 7), generator=torch.Generator().manual_seed(1))
-    a = generate(m, idx, 70, temperature=0.0, pad_to=1)  # crosses block_size: the context window slides
-    b = generate(m, idx, 70, temperature=0.0, pad_to=32)
+    a = generate(m, idx, 70, temperature=0.0, pad_to=1, use_cache=False)  # crosses block_size: the window slides
+    b = generate(m, idx, 70, temperature=0.0, pad_to=32, use_cache=False)
     assert a.shape == (2, 77) and torch.equal(a, b)
     g1, g2 = torch.Generator().manual_seed(3), torch.Generator().manual_seed(3)
     s1 = generate(m, idx, 10, temperature=0.9, top_k=20, generator=g1)
@@ -39,3 +40,20 @@ def test_cli_from_tp2_checkpoint(tmp_path, capsys):
     main(["--ckpt", str(tmp_path / "ck"), "--tokens", "104,105", "--max-new-tokens", "6", "--temperature", "0",
           "--device", "cpu"])
     assert len(capsys.readouterr().out.strip().split(",")) == 8
+
+
+def test_kv_cache_matches_full_context():
+    cfg = GPTConfig(vocab_size=300, block_size=64, n_layer=2, n_head=4, n_embd=64)
+    m = GPT(cfg, SINGLE, seed=7).eval()
+    seq = torch.randint(0, 300, (3, 40), generator=torch.Generator().manual_seed(2))
+    cache = KVCache(m, 3)
+    with torch.no_grad():
+        got = [cache.forward(seq[:, :9])]  # the prompt, then one token at a time
+        got += [cache.forward(seq[:, t : t + 1]) for t in range(9, 40)]
+        full, _ = m(seq)
+    want = full[:, 8:, :300]
+    torch.testing.assert_close(torch.stack(got, dim=1), want, atol=2e-5, rtol=1e-5)
+    idx = seq[:, :5]
+    a = generate(m, idx, 80, temperature=0.0, use_cache=True)  # past block_size: full-window steps
+    b = generate(m, idx, 80, temperature=0.0, use_cache=False, pad_to=1)
+    assert a.shape == (3, 85) and torch.equal(a, b)
