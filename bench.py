@@ -327,6 +327,8 @@ def run_ours(a, cfg: BenchConfig, lay: dict, rank, world):
         status=status,
         n_params=tr.n_params,
         note=None,
+        optimizer=("Adam on fp32 masters, bf16 params; DP reduction + update fused in one NVLink kernel per bucket"
+                   if tr.fused_dp else "Adam on fp32 masters, bf16 params; NCCL bucketed all-reduce"),
     )
 
 
@@ -477,7 +479,7 @@ def main():
             "parallelism": f"dp{world}" if cfg.name == "c2" else parallelism_name(lay),
             "sequence_parallel": cfg.sp and lay["tp"] > 1,
             "recompute": cfg.recompute,
-            "optimizer": "Adam on fp32 masters, bf16 params",
+            "optimizer": res.get("optimizer", "Adam on fp32 masters, bf16 params"),
             "dp_buckets_mb": 25,
             "l2": "no flush: each step streams several GB of weights/optimizer state/activations (>> 126 MB L2)",
             "params_rank0": res["n_params"],

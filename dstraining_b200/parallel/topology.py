@@ -275,6 +275,11 @@ def peer_reachable(ctx: TPContext) -> bool:
         ok = ok and peers_addressable(infos, ctx.rank, visible, torch.cuda.can_device_access_peer)
         votes = [None] * ctx.world
         dist.all_gather_object(votes, bool(ok), group=ctx.group)
+        if not all(votes) and ctx.rank == 0 and os.environ.get("DST_PEER", "1") != "0":
+            import warnings
+
+            warnings.warn(f"ranks {list(ctx.ranks)} cannot all address each other's GPU memory "
+                          f"(hosts / GPUs: {infos}); this group uses NCCL instead of the peer-memory kernels")
         ok = all(votes)
     _PEER_OK[key] = bool(ok)
     return _PEER_OK[key]
