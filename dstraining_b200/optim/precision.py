@@ -15,7 +15,10 @@ kernel launch per step over every parameter (the reference runs
 ``torch.optim.Adam`` plus a Python loop of casts and copies). The kernel
 implements the same update as ``torch.optim.Adam`` (Kingma & Ba, Algorithm
 1 with ``eps`` added after the bias-corrected square root) and writes
-straight into ``inner.state``, so the two paths are interchangeable.
+straight into ``inner.state``, so the two paths are interchangeable. Adam
+options the kernel does not implement (``weight_decay``, coupled or
+``decoupled_weight_decay``, ``amsgrad``, ``maximize``) take the PyTorch path
+of the same step, as in the reference.
 """
 
 from __future__ import annotations
@@ -59,9 +62,13 @@ class MasterWeightOptimizer:
             st["exp_avg_sq"] = torch.zeros_like(master, memory_format=torch.preserve_format)
         return st
 
+    def _native_supports(self) -> bool:
+        group = self.inner.param_groups[0]
+        return not (group.get("amsgrad") or group.get("maximize") or group.get("weight_decay", 0.0))
+
     def step(self) -> None:
         """One Adam step on the fp32 masters, then bf16 parameters = masters."""
-        if self._native:
+        if self._native and self._native_supports():
             self._native_step()
             return
         for mp, master in zip(self.model_params, self.master_params):
@@ -72,8 +79,6 @@ class MasterWeightOptimizer:
 
     def _native_step(self) -> None:
         group = self.inner.param_groups[0]
-        if group.get("amsgrad") or group.get("maximize") or group.get("weight_decay", 0.0):
-            raise NotImplementedError("native Adam supports plain Adam (no amsgrad/maximize/weight_decay)")
         lr = float(group["lr"])
         beta1, beta2 = group["betas"]
         eps = float(group["eps"])

@@ -65,6 +65,8 @@ def add_args(p: argparse.ArgumentParser) -> argparse.ArgumentParser:
     p.add_argument("--lr-schedule", choices=["constant", "cosine"], default="constant")
     p.add_argument("--warmup-steps", type=int, default=0, help="linear learning-rate warm-up")
     p.add_argument("--min-lr", type=float, default=0.0, help="final rate of the cosine schedule")
+    p.add_argument("--weight-decay", type=float, default=0.0,
+                   help="decoupled (AdamW) weight decay; unfused optimizer paths only (0: plain Adam, as the reference)")
     p.add_argument("--grad-clip", type=float, default=0.0,
                    help="clip the global gradient norm to this value (0: off; not with the fused DP optimizer)")
     p.add_argument("--seed", type=int, default=1337)
@@ -174,15 +176,21 @@ class Trainer:
             self.opt = FusedDPAdam(
                 model, self.dp, lr=args.lr, bucket_bytes=int(args.bucket_mb * 1024 * 1024), overlap=self.pipe is None
             )
-        elif args.bf16:
-            self.opt = MasterWeightOptimizer(model.parameters(), lr=args.lr)
         else:
-            # fused Adam (one vectorised pass per tensor; on CPU about 3x faster than
-            # the multi-tensor loop, the default there); same update as torch.optim.Adam
-            self.opt = torch.optim.Adam(model.parameters(), lr=args.lr, fused=True)
+            wd = getattr(args, "weight_decay", 0.0)
+            decay = dict(weight_decay=wd, decoupled_weight_decay=True) if wd else {}
+            if args.bf16:
+                self.opt = MasterWeightOptimizer(model.parameters(), lr=args.lr, **decay)
+            else:
+                # fused Adam (one vectorised pass per tensor; on CPU about 3x faster than
+                # the multi-tensor loop, the default there); same update as torch.optim.Adam
+                self.opt = torch.optim.Adam(model.parameters(), lr=args.lr, fused=True, **decay)
         if getattr(args, "grad_clip", 0.0) and self.fused_dp:
             raise ValueError("--grad-clip needs the unfused optimizer path (the fused DP optimizer updates "
                              "inside backward); set DST_FUSED_DP=0 or --naive-dp")
+        if getattr(args, "weight_decay", 0.0) and self.fused_dp:
+            raise ValueError("--weight-decay needs the unfused optimizer path (the fused DP optimizer implements "
+                             "plain Adam); set DST_FUSED_DP=0 or --naive-dp")
         self.last_grad_norm = None
         self.reducer = None
         if self.dp.enabled and not args.naive_dp and not self.fused_dp:

@@ -29,3 +29,46 @@ def test_trainer_loss_falls(single_rank):
     losses = [tr.step(x, y) for _ in range(8)]
     assert losses[-1] < losses[0]
     assert tr.tokens_per_step == 4 * 64
+
+
+def test_weight_decay_is_adamw(single_rank):
+    """--weight-decay gives decoupled (AdamW) decay: three trainer steps equal
+    torch.optim.AdamW (same fused CPU kernel, so bitwise) on a copy of the
+    model fed the same batches."""
+    import copy
+
+    from dstraining_b200.trainer import Trainer, add_args
+
+    a = add_args(argparse.ArgumentParser()).parse_args(
+        ["--device", "cpu", "--layers", "1", "--batch", "2", "--lr", "1e-2", "--weight-decay", "0.5"])
+    tr = Trainer(a)
+    ref = copy.deepcopy(tr.model)
+    opt = torch.optim.AdamW(ref.parameters(), lr=1e-2, weight_decay=0.5, fused=True)  # the trainer's CPU kernel
+    for s in range(3):
+        x, y = tr.shard.get_batch(s)
+        tr.step(x, y)
+        opt.zero_grad(set_to_none=True)
+        ref(x, y)[1].backward()
+        opt.step()
+    for (n, p), q in zip(tr.model.named_parameters(), ref.parameters()):
+        assert torch.equal(p, q), n
+
+
+def test_master_weights_take_torch_path_for_weight_decay():
+    """Adam options the native kernel lacks run the PyTorch update of the same
+    step (the reference passes every Adam keyword to torch.optim.Adam)."""
+    from dstraining_b200.optim.precision import MasterWeightOptimizer
+
+    torch.manual_seed(0)
+    w = torch.nn.Parameter(torch.randn(64, 32).to(torch.bfloat16))
+    opt = MasterWeightOptimizer([w], lr=1e-2, weight_decay=0.1)
+    master = w.detach().float().clone().requires_grad_(True)
+    ref = torch.optim.Adam([master], lr=1e-2, weight_decay=0.1)
+    for _ in range(3):
+        g = torch.randn(64, 32).to(torch.bfloat16)
+        w.grad = g
+        master.grad = g.float()
+        opt.step()
+        ref.step()
+    torch.testing.assert_close(opt.master_params[0], master.detach(), atol=0, rtol=0)
+    assert torch.equal(w.detach(), master.detach().to(torch.bfloat16))
