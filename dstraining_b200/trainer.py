@@ -81,6 +81,9 @@ def add_args(p: argparse.ArgumentParser) -> argparse.ArgumentParser:
     p.add_argument("--ckpt-async", action="store_true",
                    help="write periodic checkpoints from a background thread (training continues)")
     p.add_argument("--jsonl", default=None, help="append per-step metrics (JSON lines) to this file")
+    p.add_argument("--bench", action="store_true",
+                   help="report device-timed throughput over the steps after --bench-warmup (max over ranks)")
+    p.add_argument("--bench-warmup", type=int, default=3, help="untimed steps before the --bench window")
     p.add_argument("--eval-data", default=None,
                    help="held-out uint16 token file ('synthetic': a separately seeded random stream)")
     p.add_argument("--eval-every", type=int, default=0, help="evaluate every N steps (0: off)")

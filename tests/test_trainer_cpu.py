@@ -72,3 +72,22 @@ def test_master_weights_take_torch_path_for_weight_decay():
         ref.step()
     torch.testing.assert_close(opt.master_params[0], master.detach(), atol=0, rtol=0)
     assert torch.equal(w.detach(), master.detach().to(torch.bfloat16))
+
+
+def test_train_bench_record(tmp_path):
+    """``train.py --bench``: one record with the device (here: host) step time
+    over the steps after the warm-up, max over ranks, and the job's tok/s."""
+    import json
+
+    from dstraining_b200.utils.launch import launch
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sink = tmp_path / "m.jsonl"
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="1")
+    argv = [os.path.join(root, "train.py"), "--dp", "2", "--layers", "1", "--heads", "2", "--embd", "32", "--block",
+            "32", "--vocab", "128", "--batch", "2", "--steps", "6", "--device", "cpu", "--bench", "--bench-warmup",
+            "2", "--log-every", "10", "--jsonl", str(sink)]
+    assert launch(2, argv, timeout=300, env=env) == 0
+    rec = [json.loads(line) for line in sink.read_text().splitlines() if "bench_steps" in line]
+    assert len(rec) == 1 and rec[0]["bench_steps"] == 4 and rec[0]["bench_ms_per_step"] > 0
+    assert abs(rec[0]["bench_tok_s"] - 2 * 32 * 2 / (rec[0]["bench_ms_per_step"] / 1e3)) < 1e-3 * rec[0]["bench_tok_s"]

@@ -8,7 +8,8 @@ parallelism, selective recompute and bf16 + fp32 master weights.
     torchrun --nproc_per_node 8 train.py --dp 8 --bf16 --vp --gpt2 --batch 16 --vocab 50304
 
 Same flags as the reference's ``train.py:29-58`` (plus ``--bucket-mb``,
-checkpointing with retention, ``--heartbeat-timeout`` and ``--jsonl``, whose records carry
+checkpointing with retention, ``--bench`` (device-timed throughput over the steps after
+``--bench-warmup``, max over ranks), ``--heartbeat-timeout`` and ``--jsonl``, whose records carry
 the loss, tok/s, the device step time max over ranks, the peak memory and
 the kernels' status word). Logs ``step N  loss X  T tok/s`` from the
 last pipeline stage's tp0/dp0 rank; the loss is averaged over DP and the
@@ -41,6 +42,34 @@ def main():
         raise
 
 
+def bench_mark(cuda: bool):
+    """A point in the device's timeline (CUDA event) or, on CPU, the host clock."""
+    if cuda:
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        return ev
+    return time.perf_counter()
+
+
+def report_bench(args, tr, start, end, steps: int, sink) -> None:
+    """``--bench``: mean step time over the timed window, max over all ranks,
+    and the whole job's tokens/s (a collective: every rank calls it)."""
+    if start is None or steps <= 0:
+        ms = float("nan")
+    elif isinstance(start, float):
+        ms = (end - start) * 1e3 / steps
+    else:
+        end.synchronize()
+        ms = start.elapsed_time(end) / steps
+    (ms,) = tr.world_max([ms])
+    if tr.is_logger:
+        tps = tr.tokens_per_step / (ms / 1e3) if ms == ms else float("nan")
+        print(f"bench  {steps} steps  {ms:.3f} ms/step (device, max over ranks)  {tps:,.0f} tok/s", flush=True)
+        if sink:
+            sink.write(json.dumps({"bench_steps": steps, "bench_ms_per_step": ms, "bench_tok_s": tps}) + "\n")
+            sink.flush()
+
+
 def prune(args) -> None:
     """Checkpoint retention (``--ckpt-keep``), by global rank 0 once a
     checkpoint is complete."""
@@ -71,8 +100,12 @@ def run(args):
     events = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) if cuda else None
     t_last, s_last = time.time(), start_step
     pending = None  # checkpoint being written in the background
+    first_timed = start_step + args.bench_warmup
+    window = None  # --bench: start/end marks around the timed steps
     for step in range(start_step, args.steps):
         maybe_inject_fault(step)
+        if args.bench and step == first_timed:
+            window = bench_mark(cuda)
         idx, tgt = tr.shard.get_batch(step, pin=cuda)
         t_step = time.perf_counter()
         if events:
@@ -127,6 +160,9 @@ def run(args):
             pending = out if args.ckpt_async else None
             if pending is None:
                 prune(args)
+    if args.bench:
+        report_bench(args, tr, window, bench_mark(cuda) if window is not None else None, args.steps - first_timed,
+                     sink)
     if pending is not None:
         pending.wait()
     if args.ckpt_dir:
