@@ -168,6 +168,41 @@ class _RecvQueue:
         return buf
 
 
+def order_1f1b(p: int, s: int, m: int) -> List[Tuple[str, int]]:
+    """Op order of stage ``s`` of ``p`` for ``m`` micro-batches: ``("F", i)``
+    runs micro-batch i forward, ``("B", i)`` backward. ``min(p - 1 - s, m)``
+    warm-up forwards, then one forward and one backward alternately, then the
+    remaining backwards (``dst/pipeline.py:138-171``)."""
+    n_warm = min(p - 1 - s, m)
+    ops = [("F", i) for i in range(n_warm)]
+    for i in range(n_warm, m):
+        ops += [("F", i), ("B", i - n_warm)]
+    ops += [("B", i) for i in range(m - n_warm, m)]
+    return ops
+
+
+def interleaved_chunk(step: int, p: int, v: int, forward: bool) -> int:
+    """Model chunk of the ``step``-th forward (backward) of a rank in the
+    interleaved schedule: groups of ``p`` steps per chunk, chunks ascending
+    forward and descending backward (``dst/pipeline.py:278-280``)."""
+    c = (step % (p * v)) // p
+    return c if forward else v - 1 - c
+
+
+def order_interleaved(p: int, r: int, v: int, m: int) -> List[Tuple[str, int]]:
+    """Op order of rank ``r`` of ``p`` with ``v`` chunks and ``m`` micro-batches:
+    ``("F", k)`` is the rank's k-th forward step, ``("B", k)`` its k-th backward
+    step (chunk from :func:`interleaved_chunk`). Warm-up depth
+    ``min(2 (p - 1 - r) + (v - 1) p, m v)`` as in ``dst/pipeline.py:269-270``."""
+    tnm = m * v
+    n_warm = min(2 * (p - 1 - r) + (v - 1) * p, tnm)
+    ops = [("F", i) for i in range(n_warm)]
+    for j in range(tnm - n_warm):
+        ops += [("F", n_warm + j), ("B", j)]
+    ops += [("B", j) for j in range(tnm - n_warm, tnm)]
+    return ops
+
+
 def _param_meta(module) -> Tuple[torch.dtype, torch.device]:
     p0 = next(module.parameters())
     return p0.dtype, p0.device
@@ -206,7 +241,6 @@ class Pipeline1F1B:
         p, s = self.pp.world, self.pp.rank
         micro_idx = idx.split(self.micro_batch_size)
         micro_tgt = targets.split(self.micro_batch_size)
-        n_warm = min(p - 1 - s, m)
         meta = (self.act_shape, self.act_dtype, self.act_device)
         fwd_q = _RecvQueue(self.fwd_in, m, *meta)
         bwd_q = _RecvQueue(self.bwd_in, m, *meta)
@@ -236,13 +270,11 @@ class Pipeline1F1B:
             if inp is not None:
                 self.bwd_out.isend(inp.grad, sent)
 
-        for i in range(n_warm):
-            forward(i)
-        for i in range(n_warm, m):
-            forward(i)
-            backward()
-        for _ in range(n_warm):
-            backward()
+        for op, i in order_1f1b(p, s, m):
+            if op == "F":
+                forward(i)
+            else:
+                backward()  # micro-batches leave the stash in order: this is micro-batch i
         for work, _ in sent:
             work.wait()
         assert not stash
@@ -315,11 +347,9 @@ class PipelineInterleaved:
         micro_idx = idx.split(self.micro_batch_size)
         micro_tgt = targets.split(self.micro_batch_size)
         tnm = m * v
-        n_warm = min(2 * (p - 1 - r) + (v - 1) * p, tnm)
 
         def chunk(step: int, forward: bool) -> int:
-            c = (step % (p * v)) // p
-            return c if forward else v - 1 - c
+            return interleaved_chunk(step, p, v, forward)
 
         # Messages each incoming link will deliver, in order: one per forward
         # (backward) step whose chunk is not virtual-first (virtual-last).
@@ -376,13 +406,11 @@ class PipelineInterleaved:
                 else:
                     local_bwd.append(inp.grad)
 
-        for i in range(n_warm):
-            fwd(i)
-        for j in range(tnm - n_warm):
-            fwd(n_warm + j)
-            bwd(j)
-        for j in range(tnm - n_warm, tnm):
-            bwd(j)
+        for op, k in order_interleaved(p, r, v, m):
+            if op == "F":
+                fwd(k)
+            else:
+                bwd(k)
         for work, _ in sent:
             work.wait()
         assert all(not q for q in stash) and fed in (0, m)
@@ -404,7 +432,7 @@ class PipelineInterleaved:
         tnm = m * v
 
         def chunk(step: int) -> int:
-            return (step % (p * v)) // p
+            return interleaved_chunk(step, p, v, True)
 
         n_fwd_in = sum(1 for i in range(tnm) if not self._is_vfirst(chunk(i)))
         meta = (self.act_shape, self.act_dtype, self.act_device)
