@@ -48,7 +48,6 @@ import statistics
 import subprocess
 import sys
 import threading
-import time
 from dataclasses import dataclass
 from typing import Callable, Optional
 

@@ -11,7 +11,6 @@ the next batch matches the parallel model's.
 
 import argparse
 import shutil
-import sys
 
 from common import Report, start
 

@@ -3,8 +3,6 @@ of the same op (inputs rounded to bf16 first, so only the kernel's own
 arithmetic is measured). Small and ragged shapes exercise the bounds paths.
 """
 
-import math
-
 import pytest
 import torch
 import torch.nn.functional as F

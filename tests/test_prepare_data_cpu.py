@@ -63,8 +63,6 @@ def test_tokenizer_json(tmp_path):
 def test_train_on_prepared_data(tmp_path):
     """prepare_data -> train.py --data train.bin --eval-data val.bin on 2 gloo
     ranks (data parallel); the held-out loss is logged."""
-    import sys
-
     from dstraining_b200.utils.launch import launch
 
     src = tmp_path / "corpus"
