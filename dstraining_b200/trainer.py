@@ -81,6 +81,9 @@ def add_args(p: argparse.ArgumentParser) -> argparse.ArgumentParser:
     p.add_argument("--ckpt-async", action="store_true",
                    help="write periodic checkpoints from a background thread (training continues)")
     p.add_argument("--jsonl", default=None, help="append per-step metrics (JSON lines) to this file")
+    p.add_argument("--profile-dir", default=None,
+                   help="write a torch.profiler Chrome trace per rank for the --profile-steps window")
+    p.add_argument("--profile-steps", default="5:3", help="START:COUNT of the profiled window")
     p.add_argument("--bench", action="store_true",
                    help="report device-timed throughput over the steps after --bench-warmup (max over ranks)")
     p.add_argument("--bench-warmup", type=int, default=3, help="untimed steps before the --bench window")

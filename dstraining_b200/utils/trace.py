@@ -1,12 +1,16 @@
-"""Optional NVTX ranges for timeline tools (``DST_NVTX=1``).
+"""Timeline tracing: NVTX ranges (``DST_NVTX=1``) and ``torch.profiler``
+windows (``train.py --profile-dir``).
 
 ``nvtx_range(name)`` is a context manager that pushes an NVTX range around
-its body when ``DST_NVTX`` is set and CUDA is available, and does nothing
-otherwise (no cost on the normal path). The trainer marks its phases
+its body when ``DST_NVTX`` is set and CUDA is available, and marks the same
+range in a running :class:`StepProfiler` window; otherwise it does nothing
+(no cost on the normal path). The trainer marks its phases
 (``forward_backward``, ``dp_reduce``, ``finalize_grads``, ``optimizer``) and
-the models mark each block, so a profiler timeline shows where a step's
-time goes. The reference has no tracing (its only timing is a cumulative
-wall-clock average in ``train.py:123-152``).
+the models mark each block, so a timeline shows where a step's time goes.
+:class:`StepProfiler` records a window of steps with ``torch.profiler`` (host
+ops and, on CUDA, every kernel) and writes one Chrome trace per rank. The
+reference has no tracing (its only timing is a cumulative wall-clock average
+in ``train.py:123-152``).
 """
 
 from __future__ import annotations
@@ -17,8 +21,11 @@ import os
 import torch
 
 
+_PROFILING = False  # a StepProfiler window is recording
+
+
 def enabled() -> bool:
-    return os.environ.get("DST_NVTX", "0") not in ("", "0") and torch.cuda.is_available()
+    return (os.environ.get("DST_NVTX", "0") not in ("", "0") and torch.cuda.is_available()) or _PROFILING
 
 
 @contextlib.contextmanager
@@ -26,8 +33,55 @@ def nvtx_range(name: str):
     if not enabled():
         yield
         return
-    torch.cuda.nvtx.range_push(name)
+    nvtx = os.environ.get("DST_NVTX", "0") not in ("", "0") and torch.cuda.is_available()
+    if nvtx:
+        torch.cuda.nvtx.range_push(name)
     try:
-        yield
+        if _PROFILING:
+            with torch.profiler.record_function(name):
+                yield
+        else:
+            yield
     finally:
-        torch.cuda.nvtx.range_pop()
+        if nvtx:
+            torch.cuda.nvtx.range_pop()
+
+
+class StepProfiler:
+    """Records steps ``[start, start + count)`` with ``torch.profiler`` and
+    writes ``<out_dir>/trace_rank<R>.json`` (Chrome trace format; open it in
+    Perfetto or chrome://tracing). Call :meth:`before` and :meth:`after`
+    around every step."""
+
+    def __init__(self, out_dir: str, start: int, count: int, rank: int, cuda: bool):
+        self.out_dir, self.start, self.end, self.rank, self.cuda = out_dir, start, start + count, rank, cuda
+        self.prof = None
+        self.path = None
+
+    def before(self, step: int) -> None:
+        global _PROFILING
+        if step == self.start:
+            acts = [torch.profiler.ProfilerActivity.CPU]
+            if self.cuda:
+                acts.append(torch.profiler.ProfilerActivity.CUDA)
+            self.prof = torch.profiler.profile(activities=acts)
+            self.prof.__enter__()
+            _PROFILING = True
+
+    def after(self, step: int) -> None:
+        if self.prof is not None and step == self.end - 1:
+            self.close()
+
+    def close(self) -> None:
+        """Stop a window still open (a run shorter than the window) and write it."""
+        global _PROFILING
+        if self.prof is None:
+            return
+        if self.cuda:
+            torch.cuda.synchronize()
+        self.prof.__exit__(None, None, None)
+        _PROFILING = False
+        os.makedirs(self.out_dir, exist_ok=True)
+        self.path = os.path.join(self.out_dir, f"trace_rank{self.rank}.json")
+        self.prof.export_chrome_trace(self.path)
+        self.prof = None

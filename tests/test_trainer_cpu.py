@@ -91,3 +91,23 @@ def test_train_bench_record(tmp_path):
     rec = [json.loads(line) for line in sink.read_text().splitlines() if "bench_steps" in line]
     assert len(rec) == 1 and rec[0]["bench_steps"] == 4 and rec[0]["bench_ms_per_step"] > 0
     assert abs(rec[0]["bench_tok_s"] - 2 * 32 * 2 / (rec[0]["bench_ms_per_step"] / 1e3)) < 1e-3 * rec[0]["bench_tok_s"]
+
+
+def test_train_profile_window(tmp_path):
+    """``train.py --profile-dir``: one Chrome trace per rank, holding the
+    trainer's phase ranges and the blocks of the profiled steps."""
+    import json
+
+    from dstraining_b200.utils.launch import launch
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="1")
+    argv = [os.path.join(root, "train.py"), "--dp", "2", "--layers", "2", "--heads", "2", "--embd", "32", "--block",
+            "32", "--vocab", "128", "--batch", "2", "--steps", "5", "--device", "cpu", "--profile-dir",
+            str(tmp_path / "prof"), "--profile-steps", "2:2", "--log-every", "10"]
+    assert launch(2, argv, timeout=300, env=env) == 0
+    for r in range(2):
+        trace = json.loads((tmp_path / "prof" / f"trace_rank{r}.json").read_text())
+        names = [e.get("name") for e in trace["traceEvents"]]
+        assert names.count("forward_backward") == 2 and names.count("optimizer") == 2
+        assert names.count("block1") == 2

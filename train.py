@@ -8,7 +8,7 @@ parallelism, selective recompute and bf16 + fp32 master weights.
     torchrun --nproc_per_node 8 train.py --dp 8 --bf16 --vp --gpt2 --batch 16 --vocab 50304
 
 Same flags as the reference's ``train.py:29-58`` (plus ``--bucket-mb``,
-checkpointing with retention, ``--bench`` (device-timed throughput over the steps after
+checkpointing with retention, ``--profile-dir`` (a ``torch.profiler`` trace per rank), ``--bench`` (device-timed throughput over the steps after
 ``--bench-warmup``, max over ranks), ``--heartbeat-timeout`` and ``--jsonl``, whose records carry
 the loss, tok/s, the device step time max over ranks, the peak memory and
 the kernels' status word). Logs ``step N  loss X  T tok/s`` from the
@@ -28,6 +28,7 @@ from dstraining_b200.ops import native
 from dstraining_b200.parallel.health import maybe_inject_fault
 from dstraining_b200.trainer import Trainer, parse_args
 from dstraining_b200.utils import checkpoint
+from dstraining_b200.utils.trace import StepProfiler
 
 
 def main():
@@ -102,10 +103,17 @@ def run(args):
     pending = None  # checkpoint being written in the background
     first_timed = start_step + args.bench_warmup
     window = None  # --bench: start/end marks around the timed steps
+    prof = None
+    if args.profile_dir:
+        p_start, p_count = (int(x) for x in args.profile_steps.split(":"))
+        prof = StepProfiler(args.profile_dir, p_start, p_count, dist.get_rank() if dist.is_initialized() else 0,
+                            cuda)
     for step in range(start_step, args.steps):
         maybe_inject_fault(step)
         if args.bench and step == first_timed:
             window = bench_mark(cuda)
+        if prof:
+            prof.before(step)
         idx, tgt = tr.shard.get_batch(step, pin=cuda)
         t_step = time.perf_counter()
         if events:
@@ -113,6 +121,8 @@ def run(args):
         loss = tr.step_device(idx.to(tr.device, non_blocking=True), tgt.to(tr.device, non_blocking=True))
         if events:
             events[1].record()
+        if prof:
+            prof.after(step)
         last = step == args.steps - 1
         logging = step % args.log_every == 0 or last
         record = None
@@ -160,6 +170,8 @@ def run(args):
             pending = out if args.ckpt_async else None
             if pending is None:
                 prune(args)
+    if prof:
+        prof.close()
     if args.bench:
         report_bench(args, tr, window, bench_mark(cuda) if window is not None else None, args.steps - first_timed,
                      sink)
