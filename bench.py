@@ -326,8 +326,10 @@ def run_ours(a, cfg: BenchConfig, lay: dict, rank, world):
         status=status,
         n_params=tr.n_params,
         note=None,
-        optimizer=("Adam on fp32 masters, bf16 params; DP reduction + update fused in one NVLink kernel per bucket"
-                   if tr.fused_dp else "Adam on fp32 masters, bf16 params; NCCL bucketed all-reduce"),
+        optimizer=("Adam on fp32 masters, bf16 params; " + (
+            "DP reduction + update fused in one NVLink kernel per bucket" if getattr(tr.opt, "transport", "") == "peer"
+            else "NCCL reduce-scatter + sharded Adam + all-gather per bucket" if tr.fused_dp
+            else "NCCL bucketed all-reduce")),
     )
 
 

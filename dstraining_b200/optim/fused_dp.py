@@ -23,19 +23,33 @@ parameters always waits for ``finalize_grads``) and makes the compute stream
 wait for the side stream. Buckets launch strictly in bucket order so every
 rank issues the same kernel sequence.
 
-Without CUDA (gloo) the same bookkeeping runs with the collective and the
-update done by PyTorch ops (all-reduce, Adam on the owned slice, all-gather):
-the CPU correctness path. The update matches ``torch.optim.Adam``.
+Transports (``transport=``, chosen automatically by default):
+
+* ``"peer"`` (CUDA, every DP rank on this host, at most 8): the fused NVLink
+  kernel above;
+* ``"collectives"`` (CUDA otherwise, e.g. DP groups spanning machines): the
+  same buckets, hooks and ZeRO-1 sharding with the group's own collectives -
+  an averaging reduce-scatter of the bucket (NCCL), the native multi-tensor
+  Adam on the owned slice, an in-place all-gather of the bf16 parameters -
+  issued on the side stream, so they still overlap the rest of backward (on
+  gloo the same steps with PyTorch ops, for tests);
+* ``"host"`` (no CUDA, gloo): all-reduce, Adam on the owned slice by PyTorch
+  ops, all-gather - the CPU correctness path.
+
+The update matches ``torch.optim.Adam``.
 """
 
 from __future__ import annotations
 
 from typing import List, Optional
 
+import contextlib
+
 import torch
 import torch.distributed as dist
 
 from ..ops import native
+from ..parallel.comm import reduce_scatter_dim
 from ..parallel.dp import build_buckets
 from ..parallel.topology import DPContext, peer_reachable
 
@@ -43,7 +57,7 @@ _ALIGN = 8  # elements per rank slice are a multiple of this (16-byte vectors)
 
 
 class _Bucket:
-    def __init__(self, params, dp: DPContext, device, dtype, late: bool, use_native: bool):
+    def __init__(self, params, dp: DPContext, device, dtype, late: bool, use_peer: bool):
         self.params = params
         self.late = late
         self.offsets, off = [], 0
@@ -55,7 +69,7 @@ class _Bucket:
         self.slice = -(-off // (n * _ALIGN)) * _ALIGN
         self.padded = self.slice * n
         esize = torch.tensor([], dtype=dtype).element_size()
-        if use_native:
+        if use_peer:
             from ..parallel.symm import PeerBuffer
 
             self.gbuf = PeerBuffer(self.padded * esize, dp, device)
@@ -74,6 +88,7 @@ class _Bucket:
         self.master = self.param[lo : lo + self.slice].float().clone()
         self.exp_avg = torch.zeros_like(self.master)
         self.exp_avg_sq = torch.zeros_like(self.master)
+        self.gshard = None if use_peer else torch.zeros(self.slice, dtype=dtype, device=device)
         self.filled = set()
         self.launched = False
 
@@ -104,6 +119,7 @@ class FusedDPAdam:
         eps: float = 1e-8,
         bucket_bytes: int = 25 * 1024 * 1024,
         overlap: bool = True,
+        transport: str = "auto",
     ):
         self.dp = dp
         self.lr, self.betas, self.eps = lr, tuple(betas), eps
@@ -111,17 +127,27 @@ class FusedDPAdam:
         p0 = self.model_params[0]
         self.device, self.dtype = p0.device, p0.dtype
         self.native = p0.is_cuda and native.enabled()
-        if self.native and (self.dtype != torch.bfloat16 or dp.world > 8):
-            raise ValueError("fused DP Adam on CUDA needs bf16 parameters and at most 8 ranks")
-        if self.native and not peer_reachable(dp):
-            raise ValueError("fused DP Adam on CUDA needs every DP rank on this host with a GPU it can address "
-                             "(CUDA IPC); use GradReducer + MasterWeightOptimizer across machines")
+        if self.native and self.dtype != torch.bfloat16:
+            raise ValueError("DP Adam on CUDA needs bf16 parameters")
+        if transport == "auto":
+            if not self.native:
+                transport = "host"
+            else:
+                # collective on the DP group the first time: every rank decides alike
+                transport = "peer" if dp.world <= 8 and peer_reachable(dp) else "collectives"
+        fits = {"peer": self.native, "collectives": True, "host": not self.native}
+        if not fits.get(transport, False):
+            raise ValueError(f"transport {transport!r} does not fit parameters on {p0.device}")
+        if transport == "peer" and (dp.world > 8 or not peer_reachable(dp)):
+            raise ValueError("the peer transport needs at most 8 DP ranks on this host, each with a GPU the "
+                             "others can address (CUDA IPC)")
+        self.transport = transport
         order = self.model_params[::-1]
         late = [p for p in order if getattr(p, "sequence_parallel_replicated", False)]
         early = [p for p in order if not getattr(p, "sequence_parallel_replicated", False)]
         groups = [(g, False) for g in build_buckets(early, bucket_bytes)] + ([(late, True)] if late else [])
         self.buckets: List[_Bucket] = [
-            _Bucket(g, dp, self.device, self.dtype, is_late, self.native) for g, is_late in groups
+            _Bucket(g, dp, self.device, self.dtype, is_late, transport == "peer") for g, is_late in groups
         ]
         self._where = {}
         for b in self.buckets:
@@ -132,12 +158,13 @@ class FusedDPAdam:
         self._stepped = False
         self.overlap = overlap
         self.defer = False  # set while accumulating gradients over micro-batches
-        if self.native:
+        self.epoch = 0
+        if transport == "peer":
             from ..parallel.symm import PeerBuffer
 
             self.flags = PeerBuffer(64 * 4, dp, self.device)
             self.done = torch.zeros(1, dtype=torch.int32, device=self.device)
-            self.epoch = 0
+        if self.native:
             self.side = torch.cuda.Stream(device=self.device)
         if overlap:
             for p in order:
@@ -175,8 +202,10 @@ class FusedDPAdam:
             self._step += 1
             self._stepped = True
         b.launched = True
-        if self.native:
+        if self.transport == "peer":
             self._launch_native(b)
+        elif self.transport == "collectives":
+            self._launch_sharded(b)
         else:
             self._launch_emulated(b)
 
@@ -192,22 +221,66 @@ class FusedDPAdam:
                 float(self._step),
             )
 
+    def _launch_sharded(self, b: _Bucket) -> None:
+        """ZeRO-1 with the group's collectives (``collectives`` transport), ordered on the
+        side stream after the compute stream's work so far: averaging
+        reduce-scatter of the bucket into this rank's slice, Adam on the slice
+        (native multi-tensor kernel on CUDA), in-place all-gather of the bf16
+        parameters."""
+        lo = self.dp.rank * b.slice
+        valid = max(0, min(b.slice, b.numel - lo))
+        cuda = self.native
+        if cuda:
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream(self.device))
+            self.side.wait_event(ev)
+        with torch.cuda.stream(self.side) if cuda else contextlib.nullcontext():
+            if not self.dp.enabled:
+                b.gshard.copy_(b.grad)
+            elif cuda:
+                dist.reduce_scatter_tensor(b.gshard, b.grad, op=dist.ReduceOp.AVG, group=self.dp.group)
+            else:
+                b.gshard.copy_(reduce_scatter_dim(b.grad, self.dp, 0) / self.dp.world)
+            if valid:
+                p_slice = b.param[lo : lo + valid]
+                if cuda:
+                    native.lib().adam_master_step(
+                        [p_slice], [b.gshard[:valid]], [b.master[:valid]], [b.exp_avg[:valid]],
+                        [b.exp_avg_sq[:valid]], self.lr, self.betas[0], self.betas[1], self.eps, float(self._step),
+                    )
+                else:
+                    self._adam(b, b.gshard[:valid].float(), valid)
+                    with torch.no_grad():
+                        p_slice.copy_(b.master[:valid])
+            if self.dp.enabled:
+                mine = b.param[lo : lo + b.slice]
+                if cuda:
+                    dist.all_gather_into_tensor(b.param, mine, group=self.dp.group)  # in place
+                else:
+                    parts = [torch.empty_like(mine) for _ in range(self.dp.world)]
+                    dist.all_gather(parts, mine.clone(), group=self.dp.group)
+                    with torch.no_grad():
+                        b.param.copy_(torch.cat(parts))
+
+    def _adam(self, b: _Bucket, gv: torch.Tensor, valid: int) -> None:
+        """Adam (PyTorch ops) on the first ``valid`` owned elements, fp32 gradient ``gv``."""
+        beta1, beta2 = self.betas
+        bc1 = 1 - beta1**self._step
+        bc2 = 1 - beta2**self._step
+        m, v, w = b.exp_avg[:valid], b.exp_avg_sq[:valid], b.master[:valid]
+        m.lerp_(gv, 1 - beta1)
+        v.mul_(beta2).addcmul_(gv, gv, value=1 - beta2)
+        denom = (v.sqrt() / (bc2**0.5)).add_(self.eps)
+        w.addcdiv_(m, denom, value=-self.lr / bc1)
+
     def _launch_emulated(self, b: _Bucket) -> None:
         g = b.grad.float()
         if self.dp.enabled:
             dist.all_reduce(g, group=self.dp.group)
         lo = self.dp.rank * b.slice
         gs = g[lo : lo + b.slice] / self.dp.world
-        beta1, beta2 = self.betas
-        bc1 = 1 - beta1**self._step
-        bc2 = 1 - beta2**self._step
         valid = max(0, min(b.slice, b.numel - lo))
-        m, v, w = b.exp_avg[:valid], b.exp_avg_sq[:valid], b.master[:valid]
-        gv = gs[:valid]
-        m.lerp_(gv, 1 - beta1)
-        v.mul_(beta2).addcmul_(gv, gv, value=1 - beta2)
-        denom = (v.sqrt() / (bc2**0.5)).add_(self.eps)
-        w.addcdiv_(m, denom, value=-self.lr / bc1)
+        self._adam(b, gs[:valid], valid)
         mine = b.master.to(self.dtype)
         if self.dp.enabled:
             parts = [torch.empty_like(mine) for _ in range(self.dp.world)]
@@ -250,7 +323,7 @@ class FusedDPAdam:
         number of bucket launches, identical on all ranks), and the status
         word must be clear. Returns the violations (empty when all hold);
         collective over the DP group when it has several ranks."""
-        if not self.native:
+        if self.transport != "peer":
             return []
         torch.cuda.synchronize(self.device)
         n = self.dp.world

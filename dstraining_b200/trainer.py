@@ -170,15 +170,14 @@ class Trainer:
             # the answer is cached before any forward pass asks for it
             topology.peer_reachable(self.tp)
             topology.peer_reachable(self.dp)
-        self.fused_dp = (
-            args.bf16 and not args.naive_dp and cuda and os.environ.get("DST_FUSED_DP", "1") != "0"
-            and self.dp.world <= 8 and topology.peer_reachable(self.dp)
-        )
+        self.fused_dp = args.bf16 and not args.naive_dp and cuda and os.environ.get("DST_FUSED_DP", "1") != "0"
         if self.fused_dp:
-            # DP reduction + fp32-master Adam + parameter all-gather in one
-            # NVLink kernel per bucket (sharded optimizer state). With a single
-            # replica the same kernel is the bucketed Adam update, launched on
-            # a side stream as backward finishes each bucket.
+            # DP reduction + fp32-master Adam + parameter all-gather per bucket,
+            # launched on a side stream as backward finishes each bucket, with
+            # the optimizer state sharded over DP: one NVLink kernel when every
+            # DP rank is on this host, the group's collectives (NCCL reduce-
+            # scatter / all-gather around the native Adam) otherwise. With a
+            # single replica the kernel is the bucketed Adam update.
             self.opt = FusedDPAdam(
                 model, self.dp, lr=args.lr, bucket_bytes=int(args.bucket_mb * 1024 * 1024), overlap=self.pipe is None
             )

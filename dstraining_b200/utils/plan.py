@@ -12,8 +12,8 @@ Takes ``train.py``'s flags and reports, without building the model:
   tcgen05 attention kernels need a sequence length that is a multiple of 128
   (64 falls back to the mma.sync kernels), head size 64 or 128; the fused
   NVLink tensor-parallel kernels need sequence shards of a multiple of 128
-  tokens and at most 8 TP ranks; the fused DP optimizer needs at most 8
-  replicas;
+  tokens and at most 8 TP ranks; the one-kernel NVLink DP optimizer needs at
+  most 8 replicas on one machine (otherwise its NCCL form runs);
 * parameters per rank (first, middle and last pipeline stage) and the bytes
   of weights, gradients and optimizer state per rank - bf16 weights and
   gradients plus fp32 master and Adam moments, which the fused DP optimizer
@@ -88,9 +88,10 @@ def plan(args) -> Dict:
                 warnings.append(f"sequence shard {seq // max(tp, 1)} not a multiple of 128: fused TP kernels "
                                 "unavailable (NCCL + GEMM path)")
         if dp > 8:
-            warnings.append("more than 8 DP replicas: the fused DP optimizer supports at most 8")
+            warnings.append("more than 8 DP replicas: the DP reduction runs as NCCL reduce-scatter / all-gather "
+                            "around the sharded Adam instead of the one-kernel NVLink path")
     per_stage = [stage_params(args, s, tp) for s in range(pp)] if not errors else []
-    fused_dp = native and not getattr(args, "naive_dp", False) and dp <= 8
+    fused_dp = native and not getattr(args, "naive_dp", False)
     mem = []
     for n in per_stage:
         weights = 2 * n if native else 4 * n
@@ -107,7 +108,8 @@ def plan(args) -> Dict:
         "errors": errors,
         "fast_path_warnings": warnings,
         "per_stage": mem,
-        "optimizer": ("fused NVLink DP Adam (state sharded over dp)" if fused_dp else
+        "optimizer": (("fused NVLink DP Adam (state sharded over dp)" if dp <= 8 else
+                       "NCCL reduce-scatter + Adam sharded over dp + all-gather") if fused_dp else
                       "fp32-master Adam" if native else "torch Adam (fp32)"),
     }
 

@@ -3,7 +3,9 @@
     python -m dstraining_b200.utils.launch 2 tests/suites/fused_dp_suite.py --dp 2
     torchrun --nproc-per-node 2 tests/suites/fused_dp_suite.py --dp 2 --device cuda --bf16
 
-fp32 (CPU emulation path): every rank trains its slice of the global batch
+fp32 (CPU: the host transport, or ``--transport collectives``, the sharded
+reduce-scatter / all-gather path that DP groups spanning machines use on
+GPUs): every rank trains its slice of the global batch
 with FusedDPAdam; the loss trajectory and final weights must match a
 single-process model trained with torch.optim.Adam on the full batch.
 bf16 on CUDA (the native NVLink kernel): the same run must track the unfused
@@ -32,6 +34,7 @@ def main():
     ap.add_argument("--sp", action="store_true")
     ap.add_argument("--bf16", action="store_true")
     ap.add_argument("--device", default=None)
+    ap.add_argument("--transport", default="auto", help="FusedDPAdam transport (auto, peer, collectives, host)")
     a = ap.parse_args()
     device = start(a.device)
     tp, pp, dp = topology.make_topology(a.tp, 1, a.dp)
@@ -49,7 +52,8 @@ def main():
         return m.to(dtype)
 
     model = build()
-    opt = FusedDPAdam(model, dp, lr=1e-3, bucket_bytes=1 << 16)
+    opt = FusedDPAdam(model, dp, lr=1e-3, bucket_bytes=1 << 16, transport=a.transport)
+    rep.say(f"transport {opt.transport}")
     rep.flag(f"{len(opt.buckets)} buckets", len(opt.buckets) > 2)
     if a.bf16:
         ref = build()

@@ -97,7 +97,9 @@ def test_train_cli_all_axes_and_resume(tmp_path):
     assert rec["step"] == 5 and rec["status"] == 0 and rec["step_ms_max"] > 0 and rec["tok_s"] > 0
 
 
-@pytest.mark.parametrize("n,args", [(2, ("--dp", "2")), (4, ("--dp", "2", "--tp", "2", "--sp")), (4, ("--dp", "4",))])
+@pytest.mark.parametrize("n,args", [(2, ("--dp", "2")), (4, ("--dp", "2", "--tp", "2", "--sp")), (4, ("--dp", "4",)),
+                                    (4, ("--dp", "4", "--transport", "collectives")),
+                                    (4, ("--dp", "2", "--tp", "2", "--sp", "--transport", "collectives"))])
 def test_fused_dp_suite(n, args):
     run(n, "fused_dp_suite.py", *args)
 
