@@ -1,6 +1,9 @@
-"""Export a trained model in the Hugging Face GPT-2 layout, for serving stacks.
+"""Export a trained model in the Hugging Face GPT-2 layout, for serving stacks,
+and import GPT-2 weights in that layout, for fine-tuning.
 
     python -m dstraining_b200.utils.export_hf --ckpt ckpt/ --out gpt2-export [--dtype bfloat16]
+    python -m dstraining_b200.utils.export_hf --import-hf gpt2-dir --ckpt ckpt/
+        # then: train.py --ckpt-dir ckpt/ --resume ... (any layout; resharded on load)
 
 Writes ``config.json`` and ``model.safetensors`` that
 ``transformers.GPT2LMHeadModel.from_pretrained(out)`` loads (and the serving
@@ -30,6 +33,7 @@ from typing import Dict
 import torch
 
 from ..models.gpt import GPT
+from ..parallel.topology import SINGLE
 
 
 def hf_config(model: GPT) -> Dict:
@@ -110,14 +114,76 @@ def export(model: GPT, out_dir: str, dtype: torch.dtype = torch.float32) -> str:
     return out_dir
 
 
-def main(argv=None) -> None:
-    from .generate import load_model
+def import_hf(hf_dir: str, seed: int = 0) -> GPT:
+    """A single-process :class:`GPT` (fp32) holding the weights of a Hugging
+    Face GPT-2 directory (``config.json`` + ``model.safetensors``; an untied
+    or tied head). The inverse of :func:`export`; the padded head rows are
+    zero."""
+    from safetensors.torch import load_file
 
-    ap = argparse.ArgumentParser(description="export a checkpoint in the Hugging Face GPT-2 layout")
-    ap.add_argument("--ckpt", required=True, help="a checkpoint directory, or a root (its latest complete one)")
-    ap.add_argument("--out", required=True)
+    from ..models.gpt import GPTConfig
+
+    with open(os.path.join(hf_dir, "config.json")) as f:
+        conf = json.load(f)
+    if conf.get("activation_function", "gelu_new") not in ("gelu_new", "gelu_pytorch_tanh"):
+        raise ValueError(f"activation {conf.get('activation_function')!r}: this model uses tanh GELU")
+    if conf.get("n_inner") not in (None, 4 * conf["n_embd"]):
+        raise ValueError("n_inner must be 4 * n_embd")
+    cfg = GPTConfig(vocab_size=conf["vocab_size"], block_size=conf["n_positions"], n_layer=conf["n_layer"],
+                    n_head=conf["n_head"], n_embd=conf["n_embd"])
+    sd = load_file(os.path.join(hf_dir, "model.safetensors"))
+    sd = {k if k.startswith(("transformer.", "lm_head.")) else "transformer." + k: v for k, v in sd.items()}
+    model = GPT(cfg, SINGLE, seed=seed)
+    rows = _qkv_rows(cfg.n_head, cfg.n_embd // cfg.n_head)
+    inv = torch.empty_like(rows)
+    inv[rows] = torch.arange(rows.numel())
+
+    def get(name: str) -> torch.Tensor:
+        return sd[name].float()
+
+    with torch.no_grad():
+        model.wte.weight.copy_(get("transformer.wte.weight"))
+        model.wpe.weight.copy_(get("transformer.wpe.weight"))
+        for i, blk in enumerate(model.blocks):
+            pre = f"transformer.h.{i}."
+            blk.ln_1.weight.copy_(get(pre + "ln_1.weight"))
+            blk.ln_1.bias.copy_(get(pre + "ln_1.bias"))
+            blk.attn.qkv.weight.copy_(get(pre + "attn.c_attn.weight").t()[inv])
+            blk.attn.qkv.bias.copy_(get(pre + "attn.c_attn.bias")[inv])
+            blk.attn.proj.weight.copy_(get(pre + "attn.c_proj.weight").t())
+            blk.attn.proj.bias.copy_(get(pre + "attn.c_proj.bias"))
+            blk.ln_2.weight.copy_(get(pre + "ln_2.weight"))
+            blk.ln_2.bias.copy_(get(pre + "ln_2.bias"))
+            blk.mlp.c_fc.weight.copy_(get(pre + "mlp.c_fc.weight").t())
+            blk.mlp.c_fc.bias.copy_(get(pre + "mlp.c_fc.bias"))
+            blk.mlp.c_proj.weight.copy_(get(pre + "mlp.c_proj.weight").t())
+            blk.mlp.c_proj.bias.copy_(get(pre + "mlp.c_proj.bias"))
+        model.ln_f.weight.copy_(get("transformer.ln_f.weight"))
+        model.ln_f.bias.copy_(get("transformer.ln_f.bias"))
+        head = sd.get("lm_head.weight", sd["transformer.wte.weight"]).float()  # tied checkpoints have no head
+        model.lm_head.weight.zero_()
+        model.lm_head.weight[: cfg.vocab_size].copy_(head)
+    return model
+
+
+def main(argv=None) -> None:
+    from . import checkpoint
+    from .generate import load_model
+    from ..parallel.topology import PP_SINGLE
+
+    ap = argparse.ArgumentParser(description="export to / import from the Hugging Face GPT-2 layout")
+    ap.add_argument("--ckpt", required=True,
+                    help="export: a checkpoint directory or root; import: the root to write a step-0 checkpoint to")
+    ap.add_argument("--out", default=None, help="export: the output directory")
+    ap.add_argument("--import-hf", default=None, help="import: a Hugging Face GPT-2 directory")
     ap.add_argument("--dtype", default="float32", choices=["float32", "bfloat16", "float16"])
     a = ap.parse_args(argv)
+    if a.import_hf:
+        model = import_hf(a.import_hf)
+        print(checkpoint.save(a.ckpt, 0, model, None, SINGLE, PP_SINGLE, SINGLE, model.config, 0))
+        return
+    if not a.out:
+        ap.error("--out is required for an export")
     model = load_model(a.ckpt)
     print(export(model, a.out, getattr(torch, a.dtype)))
 

@@ -42,3 +42,30 @@ def test_cli_from_tp2_checkpoint(tmp_path):
     hf = GPT2LMHeadModel.from_pretrained(str(tmp_path / "hf"))
     assert hf.config.vocab_size == 257 and hf.lm_head.weight.shape == (257, 32)
     assert hf.lm_head.weight.data_ptr() != hf.transformer.wte.weight.data_ptr()
+
+
+def test_import_transformers_model(tmp_path):
+    """A GPT-2 saved by transformers (tied head) imports with the same logits,
+    and fine-tuning starts from it at another layout (tp=2, resharded)."""
+    from transformers import GPT2Config, GPT2LMHeadModel
+
+    from dstraining_b200.utils import checkpoint
+    from dstraining_b200.utils.export_hf import import_hf
+
+    torch.manual_seed(0)
+    hf = GPT2LMHeadModel(GPT2Config(vocab_size=200, n_positions=32, n_embd=32, n_layer=2, n_head=2,
+                                    resid_pdrop=0.0, embd_pdrop=0.0, attn_pdrop=0.0)).eval()
+    hf.save_pretrained(str(tmp_path / "hf"))
+    m = import_hf(str(tmp_path / "hf")).eval()
+    idx = torch.randint(0, 200, (2, 32), generator=torch.Generator().manual_seed(1))
+    with torch.no_grad():
+        torch.testing.assert_close(m(idx)[0][..., :200], hf(idx).logits, atol=2e-5, rtol=1e-5)
+    main(["--import-hf", str(tmp_path / "hf"), "--ckpt", str(tmp_path / "ck")])
+    assert checkpoint.latest(str(tmp_path / "ck")).endswith("step_00000000")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="1")
+    argv = [os.path.join(root, "train.py"), "--tp", "2", "--layers", "2", "--heads", "2", "--embd", "32",
+            "--block", "32", "--vocab", "200", "--batch", "2", "--steps", "2", "--device", "cpu",
+            "--ckpt-dir", str(tmp_path / "ck"), "--resume"]
+    assert launch(2, argv, timeout=300, env=env) == 0
+    assert checkpoint.latest(str(tmp_path / "ck")).endswith("step_00000002")
