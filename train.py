@@ -5,7 +5,7 @@ parallelism, selective recompute and bf16 + fp32 master weights.
     python -m dstraining_b200.utils.launch 8 train.py --dp 2 --pp 2 --tp 2 --chunks 2 \
         --sp --recompute --steps 20 --data synthetic
     # 8 B200s, GPT-2 124M data parallel, bf16 + fp32 masters:
-    torchrun --nproc_per_node 8 train.py --dp 8 --bf16 --vp --gpt2 --batch 16 --vocab 50304
+    torchrun --nproc_per_node 8 train.py --dp 8 --bf16 --vp --gpt2 --batch 16
 
 Same flags as the reference's ``train.py:29-58`` (plus ``--bucket-mb``,
 checkpointing with retention, ``--profile-dir`` (a ``torch.profiler`` trace per rank), ``--bench`` (device-timed throughput over the steps after
