@@ -4,7 +4,9 @@
         --max-new-tokens 64 [--temperature 0.8 --top-k 40 --seed 0]
 
 ``generate(model, idx, ...)`` extends ``idx`` [B, T] token by token.
-``temperature == 0`` is greedy decoding.
+``temperature == 0`` is greedy decoding; otherwise tokens are sampled,
+optionally from the ``top_k`` most probable and / or the nucleus of
+probability ``top_p``.
 
 * With ``use_cache=True`` (the default; single-process models) the prompt is
   run once and every later token costs one row per layer: its key and value
@@ -88,7 +90,8 @@ class KVCache:
         return F.linear(x, m.lm_head.weight)[:, : cfg.vocab_size]
 
 
-def _sample(logits: torch.Tensor, temperature: float, top_k: Optional[int], generator) -> torch.Tensor:
+def _sample(logits: torch.Tensor, temperature: float, top_k: Optional[int], generator,
+            top_p: Optional[float] = None) -> torch.Tensor:
     logits = logits.float()
     if temperature <= 0:
         return logits.argmax(dim=-1, keepdim=True)
@@ -97,6 +100,13 @@ def _sample(logits: torch.Tensor, temperature: float, top_k: Optional[int], gene
         kth = torch.topk(logits, top_k, dim=-1).values[:, -1:]
         logits = logits.masked_fill(logits < kth, float("-inf"))
     probs = torch.softmax(logits, dim=-1)
+    if top_p is not None and top_p < 1.0:
+        # nucleus: the most probable tokens whose probabilities sum to top_p (at least one)
+        sorted_p, order = probs.sort(dim=-1, descending=True)
+        drop = sorted_p.cumsum(dim=-1) - sorted_p >= top_p
+        sorted_p = sorted_p.masked_fill(drop, 0.0)
+        probs = torch.zeros_like(probs).scatter_(-1, order, sorted_p)
+        probs = probs / probs.sum(dim=-1, keepdim=True)
     return torch.multinomial(probs.cpu(), 1, generator=generator).to(logits.device)
 
 
@@ -114,7 +124,7 @@ def _full_context_logits(model: GPT, idx: torch.Tensor, pad_to: int) -> torch.Te
 @torch.no_grad()
 def generate(model: GPT, idx: torch.Tensor, max_new_tokens: int, temperature: float = 1.0,
              top_k: Optional[int] = None, generator: Optional[torch.Generator] = None, pad_to: int = 128,
-             use_cache: bool = True) -> torch.Tensor:
+             use_cache: bool = True, top_p: Optional[float] = None) -> torch.Tensor:
     cfg = model.config
     cache = KVCache(model, idx.shape[0]) if (use_cache and not model.tp.enabled) else None
     was_training = model.training
@@ -127,7 +137,7 @@ def generate(model: GPT, idx: torch.Tensor, max_new_tokens: int, temperature: fl
                 logits = cache.forward(idx)
             else:
                 logits = cache.forward(idx[:, -1:])
-            nxt = _sample(logits, temperature, top_k, generator)
+            nxt = _sample(logits, temperature, top_k, generator, top_p)
             idx = torch.cat([idx, nxt.to(idx.dtype)], dim=1)
     finally:
         model.train(was_training)
@@ -160,6 +170,7 @@ def main(argv=None) -> None:
     ap.add_argument("--max-new-tokens", type=int, default=64)
     ap.add_argument("--temperature", type=float, default=1.0)
     ap.add_argument("--top-k", type=int, default=None)
+    ap.add_argument("--top-p", type=float, default=None, help="nucleus sampling")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--device", default="cuda" if torch.cuda.is_available() else "cpu")
     a = ap.parse_args(argv)
@@ -179,7 +190,7 @@ def main(argv=None) -> None:
             else (lambda out: tok.tok.decode(out))
     idx = torch.tensor([ids], dtype=torch.long, device=a.device)
     g = torch.Generator().manual_seed(a.seed)
-    out = generate(model, idx, a.max_new_tokens, a.temperature, a.top_k, g)[0].tolist()
+    out = generate(model, idx, a.max_new_tokens, a.temperature, a.top_k, g, top_p=a.top_p)[0].tolist()
     print(decode(out) if decode else ",".join(map(str, out)))
 
 

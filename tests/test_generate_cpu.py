@@ -57,3 +57,14 @@ def test_kv_cache_matches_full_context():
     a = generate(m, idx, 80, temperature=0.0, use_cache=True)  # past block_size: full-window steps
     b = generate(m, idx, 80, temperature=0.0, use_cache=False, pad_to=1)
     assert a.shape == (3, 85) and torch.equal(a, b)
+
+
+def test_top_p_keeps_the_nucleus():
+    from dstraining_b200.utils.generate import _sample
+
+    logits = torch.log(torch.tensor([[0.5, 0.3, 0.15, 0.05]]))
+    g = torch.Generator().manual_seed(0)
+    draws = {int(_sample(logits, 1.0, None, g, top_p=0.7)) for _ in range(200)}
+    assert draws == {0, 1}  # 0.5 + 0.3 covers 0.7; tokens 2 and 3 are cut
+    draws = {int(_sample(logits, 1.0, None, g, top_p=0.1)) for _ in range(50)}
+    assert draws == {0}  # always at least the most probable token
