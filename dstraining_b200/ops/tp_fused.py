@@ -58,14 +58,15 @@ class _Channel:
         return self.buf.view(torch.bfloat16)[:numel]
 
 
-_CHANNELS: Dict[Tuple[int, str], _Channel] = {}
+_CHANNELS: Dict[Tuple[int, str, Tuple[int, ...]], _Channel] = {}
 
 
 def channel(owner: int, role: str, tp: TPContext, nbytes: int, device: torch.device) -> _Channel:
     """The channel of one call site, keyed by the owning layer (the id of its
-    weight Parameter, captured in forward) and a role; created or grown
+    weight Parameter, captured in forward), a role and the group's ranks (an
+    id can be reused by a later model in another group); created or grown
     collectively in program order."""
-    key = (owner, role)
+    key = (owner, role, tuple(tp.ranks))
     ch = _CHANNELS.get(key)
     if ch is None or ch.nbytes < nbytes:
         ch = _Channel(tp, device, nbytes)
