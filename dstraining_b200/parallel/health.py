@@ -27,11 +27,13 @@ from __future__ import annotations
 
 import datetime
 import os
+import signal
 import sys
 import threading
 import time
 from typing import Callable, List, Optional
 
+import torch
 import torch.distributed as dist
 
 _PREFIX = "dst/health"
@@ -217,6 +219,36 @@ def maybe_inject_fault(step: int) -> None:
         with open(once, "w") as f:
             f.write(f"rank {rank} step {step}\n")
     raise RuntimeError(f"injected fault on rank {rank} at step {step}")
+
+
+class StopRequest:
+    """Preemption handling: SIGTERM / SIGUSR1 set a flag; :meth:`agreed`
+    (a collective over all ranks) tells every rank, at the same step, that at
+    least one of them was signalled, so they can checkpoint together and
+    exit. ``DST_INJECT_SIGNAL="<rank>:<step>"`` makes that rank signal itself
+    at that step (for tests)."""
+
+    def __init__(self, signals=(signal.SIGTERM, signal.SIGUSR1)):
+        self.flag = False
+        for sig in signals:
+            signal.signal(sig, self._handler)
+
+    def _handler(self, signum, frame) -> None:  # noqa: ARG002 - signal handler signature
+        self.flag = True
+
+    def maybe_inject(self, step: int) -> None:
+        spec = os.environ.get("DST_INJECT_SIGNAL")
+        if spec:
+            rank, at = (int(v) for v in spec.split(":"))
+            if step == at and (not dist.is_initialized() or dist.get_rank() == rank):
+                os.kill(os.getpid(), signal.SIGTERM)
+
+    def agreed(self, device: torch.device) -> bool:
+        """Whether any rank was signalled (collective: every rank calls it at the same step)."""
+        t = torch.tensor([1.0 if self.flag else 0.0], device=device)
+        if dist.is_initialized() and dist.get_world_size() > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return bool(t.item() > 0)
 
 
 def start_monitoring(interval: float = 1.0, timeout: float = 10.0):

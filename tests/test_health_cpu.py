@@ -48,3 +48,25 @@ def test_step_gate_raises_on_missing_rank(one_rank):
     with pytest.raises(health.PeerFailure, match=r"\[1\] did not reach step 0"):
         gate.enter(0)
     assert time.time() - t0 < 5
+
+
+def test_save_on_signal_then_resume(tmp_path):
+    """--save-on-signal: rank 1 receives SIGTERM during step 3; at the next
+    agreed check (after step 3) every rank checkpoints step 4 and exits 0;
+    --resume continues from it to the end."""
+    import os
+
+    from dstraining_b200.utils import checkpoint
+    from dstraining_b200.utils.launch import launch
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    ck = str(tmp_path / "ck")
+    common = [os.path.join(root, "train.py"), "--dp", "2", "--layers", "1", "--heads", "2", "--embd", "32",
+              "--block", "32", "--vocab", "128", "--batch", "2", "--steps", "12", "--device", "cpu",
+              "--ckpt-dir", ck, "--save-on-signal", "--signal-check-every", "2"]
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="1", DST_INJECT_SIGNAL="1:3")
+    assert launch(2, common, timeout=300, env=env) == 0
+    assert checkpoint.latest(ck).endswith("step_00000004")
+    env.pop("DST_INJECT_SIGNAL")
+    assert launch(2, [*common, "--resume"], timeout=300, env=env) == 0
+    assert checkpoint.latest(ck).endswith("step_00000012")

@@ -8,7 +8,7 @@ parallelism, selective recompute and bf16 + fp32 master weights.
     torchrun --nproc_per_node 8 train.py --dp 8 --bf16 --vp --gpt2 --batch 16
 
 Same flags as the reference's ``train.py:29-58`` (plus ``--bucket-mb``,
-checkpointing with retention, ``--profile-dir`` (a ``torch.profiler`` trace per rank), ``--bench`` (device-timed throughput over the steps after
+checkpointing with retention and ``--save-on-signal`` (preemption), ``--profile-dir`` (a ``torch.profiler`` trace per rank), ``--bench`` (device-timed throughput over the steps after
 ``--bench-warmup``, max over ranks), ``--heartbeat-timeout`` and ``--jsonl``, whose records carry
 the loss, tok/s, the device step time max over ranks, the peak memory and
 the kernels' status word). Logs ``step N  loss X  T tok/s`` from the
@@ -25,7 +25,7 @@ import torch
 import torch.distributed as dist
 
 from dstraining_b200.ops import native
-from dstraining_b200.parallel.health import maybe_inject_fault
+from dstraining_b200.parallel.health import StopRequest, maybe_inject_fault
 from dstraining_b200.trainer import Trainer, parse_args
 from dstraining_b200.utils import checkpoint
 from dstraining_b200.utils.trace import StepProfiler
@@ -103,6 +103,9 @@ def run(args):
     pending = None  # checkpoint being written in the background
     first_timed = start_step + args.bench_warmup
     window = None  # --bench: start/end marks around the timed steps
+    stop = StopRequest() if args.save_on_signal else None
+    if stop and not args.ckpt_dir:
+        raise SystemExit("--save-on-signal needs --ckpt-dir")
     prof = None
     if args.profile_dir:
         p_start, p_count = (int(x) for x in args.profile_steps.split(":"))
@@ -161,6 +164,24 @@ def run(args):
                 if sink:
                     sink.write(json.dumps({"step": step, "eval_loss": ev}) + "\n")
                     sink.flush()
+        if stop is not None:
+            stop.maybe_inject(step)
+            if ((step + 1) % max(1, args.signal_check_every) == 0 or last) and stop.agreed(tr.device):
+                if pending is not None:
+                    pending.wait()
+                path = checkpoint.save(args.ckpt_dir, step + 1, tr.model, tr.opt, tr.tp, tr.pp, tr.dp, tr.config,
+                                       args.seed)
+                prune(args)
+                if tr.is_logger:
+                    print(f"signal received: saved {path} after step {step}; exiting", flush=True)
+                if prof:
+                    prof.close()
+                if sink:
+                    sink.close()
+                if dist.is_initialized():
+                    dist.barrier()
+                    dist.destroy_process_group()
+                sys.exit(0)
         if args.ckpt_dir and args.ckpt_every and (step + 1) % args.ckpt_every == 0 and not last:
             if pending is not None:
                 pending.wait()  # one background write at a time
