@@ -80,8 +80,10 @@ def add_args(p: argparse.ArgumentParser) -> argparse.ArgumentParser:
                    help="keep only the newest N complete checkpoints (0: keep all)")
     p.add_argument("--save-on-signal", action="store_true",
                    help="on SIGTERM / SIGUSR1 to any rank: checkpoint at the next agreed step and exit 0")
+    p.add_argument("--time-limit-min", type=float, default=0.0,
+                   help="checkpoint and exit 0 once this much wall time has passed (0: off; needs --ckpt-dir)")
     p.add_argument("--signal-check-every", type=int, default=10,
-                   help="steps between the (collective) checks for a pending signal")
+                   help="steps between the (collective) checks for a pending signal or time limit")
     p.add_argument("--ckpt-async", action="store_true",
                    help="write periodic checkpoints from a background thread (training continues)")
     p.add_argument("--jsonl", default=None, help="append per-step metrics (JSON lines) to this file")

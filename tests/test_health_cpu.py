@@ -70,3 +70,19 @@ def test_save_on_signal_then_resume(tmp_path):
     env.pop("DST_INJECT_SIGNAL")
     assert launch(2, [*common, "--resume"], timeout=300, env=env) == 0
     assert checkpoint.latest(ck).endswith("step_00000012")
+
+
+def test_time_limit_checkpoints_and_exits(tmp_path):
+    import os
+
+    from dstraining_b200.utils import checkpoint
+    from dstraining_b200.utils.launch import launch
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    ck = str(tmp_path / "ck")
+    argv = [os.path.join(root, "train.py"), "--layers", "1", "--heads", "2", "--embd", "32", "--block", "32",
+            "--vocab", "128", "--batch", "2", "--steps", "100000", "--device", "cpu", "--ckpt-dir", ck,
+            "--time-limit-min", "0.0001", "--signal-check-every", "3"]
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="1")
+    assert launch(1, argv, timeout=300, env=env) == 0
+    assert checkpoint.latest(ck).endswith("step_00000003")  # the first check, past 6 ms

@@ -103,9 +103,10 @@ def run(args):
     pending = None  # checkpoint being written in the background
     first_timed = start_step + args.bench_warmup
     window = None  # --bench: start/end marks around the timed steps
-    stop = StopRequest() if args.save_on_signal else None
+    stop = StopRequest() if (args.save_on_signal or args.time_limit_min) else None
     if stop and not args.ckpt_dir:
-        raise SystemExit("--save-on-signal needs --ckpt-dir")
+        raise SystemExit("--save-on-signal / --time-limit-min need --ckpt-dir")
+    t_start = time.time()
     prof = None
     if args.profile_dir:
         p_start, p_count = (int(x) for x in args.profile_steps.split(":"))
@@ -166,6 +167,8 @@ def run(args):
                     sink.flush()
         if stop is not None:
             stop.maybe_inject(step)
+            if args.time_limit_min and time.time() - t_start > args.time_limit_min * 60:
+                stop.flag = True
             if ((step + 1) % max(1, args.signal_check_every) == 0 or last) and stop.agreed(tr.device):
                 if pending is not None:
                     pending.wait()
@@ -173,7 +176,8 @@ def run(args):
                                        args.seed)
                 prune(args)
                 if tr.is_logger:
-                    print(f"signal received: saved {path} after step {step}; exiting", flush=True)
+                    print(f"stop requested (signal or time limit): saved {path} after step {step}; exiting",
+                          flush=True)
                 if prof:
                     prof.close()
                 if sink:
