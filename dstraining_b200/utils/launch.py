@@ -13,7 +13,8 @@ rendezvous) with the restart arguments appended, up to K times - with
 ``train.py --ckpt-dir ... --ckpt-every ...`` this resumes from the latest
 complete checkpoint, the recovery path after a rank failure. With
 ``--restart-nproc M`` (and layout flags in ``--restart-args``) the job comes
-back on M ranks: checkpoints are resharded on load.
+back on M ranks: checkpoints are resharded on load. SIGTERM / SIGUSR1 to the
+launcher go to every rank, and a job stopped that way is not restarted.
 """
 
 from __future__ import annotations
@@ -29,9 +30,14 @@ import time
 from typing import List, Optional, Sequence
 
 
+_FORWARDED: List[int] = []  # signals passed on to the ranks (a preempted job is not restarted)
+
+
 def launch(nproc: int, argv: List[str], timeout: Optional[float] = None, env: Optional[dict] = None) -> int:
     """Run ``nproc`` ranks of ``python argv``; 0 if every rank exits 0, else 1
-    (survivors are killed when one fails or the timeout expires)."""
+    (survivors are killed when one fails or the timeout expires). SIGTERM and
+    SIGUSR1 sent to the launcher are passed on to every rank (with
+    ``train.py --save-on-signal`` they checkpoint together and exit 0)."""
     store_dir = tempfile.mkdtemp(prefix="dst_store_")
     store = os.path.join(store_dir, "store")
     procs = []
@@ -39,6 +45,22 @@ def launch(nproc: int, argv: List[str], timeout: Optional[float] = None, env: Op
         e = dict(os.environ if env is None else env)
         e.update(RANK=str(r), LOCAL_RANK=str(r), WORLD_SIZE=str(nproc), DST_INIT_METHOD=f"file://{store}")
         procs.append(subprocess.Popen([sys.executable, *argv], env=e, start_new_session=True))
+
+    def forward(signum, frame):  # noqa: ARG001 - signal handler signature
+        _FORWARDED.append(signum)
+        for p in procs:
+            if p.poll() is None:
+                try:
+                    os.killpg(p.pid, signum)
+                except ProcessLookupError:
+                    pass
+
+    previous = {}
+    for sig in (signal.SIGTERM, signal.SIGUSR1):
+        try:
+            previous[sig] = signal.signal(sig, forward)
+        except ValueError:  # not the main thread: leave signals alone
+            pass
     deadline = None if timeout is None else time.monotonic() + timeout
     codes = [None] * nproc
     try:
@@ -60,6 +82,8 @@ def launch(nproc: int, argv: List[str], timeout: Optional[float] = None, env: Op
         for p in procs:
             if p.poll() is None:
                 os.killpg(p.pid, signal.SIGKILL)
+        for sig, handler in previous.items():
+            signal.signal(sig, handler)
     return 0 if all(c == 0 for c in codes) else 1
 
 
@@ -77,6 +101,9 @@ def launch_with_restarts(nproc: int, argv: List[str], max_restarts: int = 0, res
         n = nproc if attempt == 0 or restart_nproc is None else restart_nproc
         if launch(n, args, timeout, env) == 0:
             return 0
+        if _FORWARDED:
+            print("[dst launch] stopped by a signal; not restarting", file=sys.stderr, flush=True)
+            return 1
         if attempt < max_restarts:
             print(f"[dst launch] job failed; restart {attempt + 1} of {max_restarts}", file=sys.stderr, flush=True)
     return 1

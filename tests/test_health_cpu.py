@@ -86,3 +86,37 @@ def test_time_limit_checkpoints_and_exits(tmp_path):
     env = dict(os.environ, CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="1")
     assert launch(1, argv, timeout=300, env=env) == 0
     assert checkpoint.latest(ck).endswith("step_00000003")  # the first check, past 6 ms
+
+
+def test_launcher_forwards_sigterm(tmp_path):
+    """SIGTERM to the launcher reaches every rank; with --save-on-signal the
+    job checkpoints at an agreed step and the launcher exits 0."""
+    import os
+    import signal
+    import subprocess
+    import sys
+    import time
+
+    from dstraining_b200.utils import checkpoint
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    ck = str(tmp_path / "ck")
+    sink = tmp_path / "m.jsonl"
+    cmd = [sys.executable, "-m", "dstraining_b200.utils.launch", "--timeout", "240", "2",
+           os.path.join(root, "train.py"), "--dp", "2", "--layers", "1", "--heads", "2", "--embd", "32", "--block",
+           "32", "--vocab", "128", "--batch", "2", "--steps", "100000", "--device", "cpu", "--ckpt-dir", ck,
+           "--save-on-signal", "--signal-check-every", "2", "--jsonl", str(sink)]
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="1",
+               PYTHONPATH=root + os.pathsep + os.environ.get("PYTHONPATH", ""))
+    p = subprocess.Popen(cmd, env=env, cwd=root)
+    try:
+        t0 = time.time()
+        while not (sink.exists() and len(sink.read_text().splitlines()) >= 3):
+            assert p.poll() is None and time.time() - t0 < 120
+            time.sleep(0.2)
+        p.send_signal(signal.SIGTERM)
+        assert p.wait(timeout=120) == 0
+    finally:
+        if p.poll() is None:
+            p.kill()
+    assert checkpoint.latest(ck) is not None
