@@ -68,3 +68,30 @@ def test_reference_train_script_runs_on_our_dst(tmp_path):
     args = ["--dp", "2", "--tp", "2", "--pp", "2", "--chunks", "2", "--sp", "--vp", "--recompute", "--bf16",
             "--micro", "2", "--steps", "4", "--data", "synthetic", "--device", "cpu"]
     assert launch(8, [str(tmp_path / "train.py"), *args], timeout=600, env=_env()) == 0
+
+
+def test_every_public_name_of_the_reference_modules():
+    """Each name a reference ``dst`` module defines at top level (functions,
+    classes, constants; plus ``_Recompute``, which its tests patch) exists in
+    the module of the same name here. Read from the reference's source as
+    text (AST), so nothing of it is imported."""
+    import ast
+    import importlib
+
+    ref_pkg = os.path.join(ROOT, "baseline", "_ref", "dst")
+    missing = []
+    for fname in sorted(os.listdir(ref_pkg)):
+        if not fname.endswith(".py") or fname == "__init__.py":
+            continue
+        with open(os.path.join(ref_pkg, fname)) as f:
+            tree = ast.parse(f.read())
+        names = set()
+        for node in tree.body:
+            if isinstance(node, (ast.FunctionDef, ast.ClassDef)):
+                names.add(node.name)
+            elif isinstance(node, ast.Assign):
+                names.update(t.id for t in node.targets if isinstance(t, ast.Name))
+        public = {n for n in names if not n.startswith("_")} | ({"_Recompute"} & names)
+        ours = importlib.import_module(f"dst.{fname[:-3]}")
+        missing += [f"dst.{fname[:-3]}.{n}" for n in sorted(public) if not hasattr(ours, n)]
+    assert not missing, missing
