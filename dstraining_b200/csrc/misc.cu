@@ -120,11 +120,13 @@ struct AdamTable {
 
 constexpr int kAdamChunk = 4096;
 
-// Adam (Kingma & Ba) on fp32 masters with bf16 params/grads:
+// Adam (Kingma & Ba) on fp32 masters with bf16 params/grads, with decoupled
+// weight decay (Loshchilov & Hutter, AdamW) as the factor `decay` = 1 - lr*wd:
 //   m = b1 m + (1-b1) g;  v = b2 v + (1-b2) g^2
-//   master -= (lr / bc1) * m / (sqrt(v) / sqrt(bc2) + eps);  param = bf16(master)
+//   master = master * decay - (lr / bc1) * m / (sqrt(v) / sqrt(bc2) + eps);  param = bf16(master)
+// decay == 1 is plain Adam.
 __global__ void adam_kernel(const __grid_constant__ AdamTable tab, float lr, float beta1, float beta2, float eps,
-                            float step_size, float inv_sqrt_bc2) {
+                            float step_size, float inv_sqrt_bc2, float decay) {
   const int64_t chunk = blockIdx.x;
   int lo = 0, hi = tab.count - 1;
   while (lo < hi) {  // last tensor whose chunk_start <= chunk
@@ -149,7 +151,7 @@ __global__ void adam_kernel(const __grid_constant__ AdamTable tab, float lr, flo
     m = m + (g - m) * (1.f - beta1);
     v = v * beta2 + (1.f - beta2) * g * g;
     const float denom = sqrtf(v) * inv_sqrt_bc2 + eps;
-    const float w = W[i] - step_size * (m / denom);
+    const float w = W[i] * decay - step_size * (m / denom);
     M[i] = m;
     Vv[i] = v;
     W[i] = w;
@@ -255,8 +257,9 @@ std::vector<at::Tensor> embedding_bwd(const at::Tensor& dy, const at::Tensor& id
 void adam_master_step(const std::vector<at::Tensor>& params, const std::vector<at::Tensor>& grads,
                       const std::vector<at::Tensor>& masters, const std::vector<at::Tensor>& m1,
                       const std::vector<at::Tensor>& m2, double lr, double beta1, double beta2, double eps,
-                      double step) {
+                      double step, double weight_decay) {
   const size_t n = params.size();
+  const float decay = static_cast<float>(1.0 - lr * weight_decay);
   TORCH_CHECK(grads.size() == n && masters.size() == n && m1.size() == n && m2.size() == n, "adam: list sizes");
   if (n == 0) return;
   c10::cuda::CUDAGuard g(params[0].device());
@@ -292,7 +295,7 @@ void adam_master_step(const std::vector<at::Tensor>& params, const std::vector<a
     if (chunks == 0) continue;
     adam_kernel<<<static_cast<unsigned>(chunks), 256, 0, st>>>(tab, static_cast<float>(lr), static_cast<float>(beta1),
                                                                static_cast<float>(beta2), static_cast<float>(eps),
-                                                               step_size, inv_sqrt_bc2);
+                                                               step_size, inv_sqrt_bc2, decay);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
 }
@@ -341,7 +344,12 @@ void register_embed(pybind11::module& m) {
 }
 
 void register_adam(pybind11::module& m) {
-  m.def("adam_master_step", &adam_master_step, "multi-tensor Adam on fp32 masters with bf16 write-back");
+  namespace py = pybind11;
+  m.def("adam_master_step", &adam_master_step,
+        "multi-tensor Adam (decoupled weight decay optional) on fp32 masters with bf16 write-back",
+        py::arg("params"), py::arg("grads"), py::arg("masters"), py::arg("exp_avg"), py::arg("exp_avg_sq"),
+        py::arg("lr"), py::arg("beta1"), py::arg("beta2"), py::arg("eps"), py::arg("step"),
+        py::arg("weight_decay") = 0.0);
 }
 
 void register_ce(pybind11::module& m) {

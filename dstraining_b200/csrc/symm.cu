@@ -80,6 +80,7 @@ struct DpArgs {
   int rank, n;
   uint32_t epoch;
   float beta1, beta2, eps, step_size, inv_sqrt_bc2, inv_n;
+  float decay;  // decoupled weight decay factor 1 - lr * wd (1: plain Adam)
   int* status;
 };
 
@@ -128,7 +129,7 @@ __global__ void __launch_bounds__(256) fused_dp_adam_kernel(const __grid_constan
           const float gj = g[j] * a.inv_n;
           mm[j] = mm[j] + (gj - mm[j]) * (1.f - a.beta1);
           vv[j] = vv[j] * a.beta2 + (1.f - a.beta2) * gj * gj;
-          w[j] = w[j] - a.step_size * (mm[j] / (sqrtf(vv[j]) * a.inv_sqrt_bc2 + a.eps));
+          w[j] = w[j] * a.decay - a.step_size * (mm[j] / (sqrtf(vv[j]) * a.inv_sqrt_bc2 + a.eps));
         }
       }
 #pragma unroll
@@ -195,7 +196,7 @@ void symm_close(int64_t ptr, int64_t device) {
 void fused_dp_adam(const std::vector<int64_t>& grad_ptrs, const std::vector<int64_t>& param_ptrs,
                    const std::vector<int64_t>& flag_ptrs, at::Tensor& master, at::Tensor& m, at::Tensor& v,
                    at::Tensor& done_ctas, int64_t slice, int64_t valid, int64_t rank, int64_t epoch, double lr,
-                   double beta1, double beta2, double eps, double step) {
+                   double beta1, double beta2, double eps, double step, double weight_decay) {
   const int n = static_cast<int>(grad_ptrs.size());
   TORCH_CHECK(n >= 1 && n <= symm::kMaxRanks && param_ptrs.size() == static_cast<size_t>(n) &&
                   flag_ptrs.size() == static_cast<size_t>(n),
@@ -224,6 +225,7 @@ void fused_dp_adam(const std::vector<int64_t>& grad_ptrs, const std::vector<int6
   a.step_size = static_cast<float>(lr / bc1);
   a.inv_sqrt_bc2 = static_cast<float>(1.0 / std::sqrt(bc2));
   a.inv_n = 1.f / n;
+  a.decay = static_cast<float>(1.0 - lr * weight_decay);
   a.status = status_ptr();
   c10::cuda::CUDAGuard g(master.device());
   const int64_t nvec = slice / 8;
@@ -236,5 +238,11 @@ void register_symm(pybind11::module& m) {
   m.def("symm_alloc", &symm_alloc, "allocate an IPC-exportable zeroed device buffer: (tensor, handle)");
   m.def("symm_open", &symm_open, "map a peer's buffer from its IPC handle; returns the device pointer");
   m.def("symm_close", &symm_close, "unmap a peer buffer");
-  m.def("fused_dp_adam", &fused_dp_adam, "fused DP bucket reduce + sharded Adam + parameter all-gather over NVLink");
+  namespace py = pybind11;
+  m.def("fused_dp_adam", &fused_dp_adam,
+        "fused DP bucket reduce + sharded Adam (decoupled weight decay optional) + parameter all-gather over NVLink",
+        py::arg("grad_ptrs"), py::arg("param_ptrs"), py::arg("flag_ptrs"), py::arg("master"), py::arg("exp_avg"),
+        py::arg("exp_avg_sq"), py::arg("done_ctas"), py::arg("slice"), py::arg("valid"), py::arg("rank"),
+        py::arg("epoch"), py::arg("lr"), py::arg("beta1"), py::arg("beta2"), py::arg("eps"), py::arg("step"),
+        py::arg("weight_decay") = 0.0);
 }

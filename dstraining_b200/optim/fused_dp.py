@@ -36,7 +36,8 @@ Transports (``transport=``, chosen automatically by default):
 * ``"host"`` (no CUDA, gloo): all-reduce, Adam on the owned slice by PyTorch
   ops, all-gather - the CPU correctness path.
 
-The update matches ``torch.optim.Adam``.
+The update matches ``torch.optim.Adam`` (``torch.optim.AdamW`` with
+``weight_decay``).
 """
 
 from __future__ import annotations
@@ -120,9 +121,11 @@ class FusedDPAdam:
         bucket_bytes: int = 25 * 1024 * 1024,
         overlap: bool = True,
         transport: str = "auto",
+        weight_decay: float = 0.0,
     ):
         self.dp = dp
         self.lr, self.betas, self.eps = lr, tuple(betas), eps
+        self.weight_decay = float(weight_decay)  # decoupled (AdamW): master *= 1 - lr * weight_decay
         self.model_params = [p for p in model.parameters() if p.requires_grad]
         p0 = self.model_params[0]
         self.device, self.dtype = p0.device, p0.dtype
@@ -218,7 +221,7 @@ class FusedDPAdam:
             native.lib().fused_dp_adam(
                 b.gbuf.ptrs, b.pbuf.ptrs, self.flags.ptrs, b.master, b.exp_avg, b.exp_avg_sq, self.done,
                 b.slice, b.numel, self.dp.rank, self.epoch, self.lr, self.betas[0], self.betas[1], self.eps,
-                float(self._step),
+                float(self._step), weight_decay=self.weight_decay,
             )
 
     def _launch_sharded(self, b: _Bucket) -> None:
@@ -247,6 +250,7 @@ class FusedDPAdam:
                     native.lib().adam_master_step(
                         [p_slice], [b.gshard[:valid]], [b.master[:valid]], [b.exp_avg[:valid]],
                         [b.exp_avg_sq[:valid]], self.lr, self.betas[0], self.betas[1], self.eps, float(self._step),
+                        weight_decay=self.weight_decay,
                     )
                 else:
                     self._adam(b, b.gshard[:valid].float(), valid)
@@ -268,6 +272,8 @@ class FusedDPAdam:
         bc1 = 1 - beta1**self._step
         bc2 = 1 - beta2**self._step
         m, v, w = b.exp_avg[:valid], b.exp_avg_sq[:valid], b.master[:valid]
+        if self.weight_decay:
+            w.mul_(1 - self.lr * self.weight_decay)
         m.lerp_(gv, 1 - beta1)
         v.mul_(beta2).addcmul_(gv, gv, value=1 - beta2)
         denom = (v.sqrt() / (bc2**0.5)).add_(self.eps)

@@ -15,10 +15,11 @@ kernel launch per step over every parameter (the reference runs
 ``torch.optim.Adam`` plus a Python loop of casts and copies). The kernel
 implements the same update as ``torch.optim.Adam`` (Kingma & Ba, Algorithm
 1 with ``eps`` added after the bias-corrected square root) and writes
-straight into ``inner.state``, so the two paths are interchangeable. Adam
-options the kernel does not implement (``weight_decay``, coupled or
-``decoupled_weight_decay``, ``amsgrad``, ``maximize``) take the PyTorch path
-of the same step, as in the reference.
+straight into ``inner.state``, so the two paths are interchangeable. The
+kernel also applies decoupled weight decay (``weight_decay`` with
+``decoupled_weight_decay=True``, i.e. AdamW); Adam options it does not
+implement (coupled ``weight_decay``, ``amsgrad``, ``maximize``) take the
+PyTorch path of the same step, as in the reference.
 """
 
 from __future__ import annotations
@@ -64,7 +65,8 @@ class MasterWeightOptimizer:
 
     def _native_supports(self) -> bool:
         group = self.inner.param_groups[0]
-        return not (group.get("amsgrad") or group.get("maximize") or group.get("weight_decay", 0.0))
+        coupled_decay = group.get("weight_decay", 0.0) and not group.get("decoupled_weight_decay", False)
+        return not (group.get("amsgrad") or group.get("maximize") or coupled_decay)
 
     def step(self) -> None:
         """One Adam step on the fp32 masters, then bf16 parameters = masters."""
@@ -97,4 +99,5 @@ class MasterWeightOptimizer:
             masters.append(master)
             m1.append(st["exp_avg"])
             m2.append(st["exp_avg_sq"])
-        native.lib().adam_master_step(params, grads, masters, m1, m2, lr, beta1, beta2, eps, step)
+        native.lib().adam_master_step(params, grads, masters, m1, m2, lr, beta1, beta2, eps, step,
+                                      weight_decay=float(group.get("weight_decay", 0.0)))

@@ -66,7 +66,7 @@ def add_args(p: argparse.ArgumentParser) -> argparse.ArgumentParser:
     p.add_argument("--warmup-steps", type=int, default=0, help="linear learning-rate warm-up")
     p.add_argument("--min-lr", type=float, default=0.0, help="final rate of the cosine schedule")
     p.add_argument("--weight-decay", type=float, default=0.0,
-                   help="decoupled (AdamW) weight decay; unfused optimizer paths only (0: plain Adam, as the reference)")
+                   help="decoupled (AdamW) weight decay (0: plain Adam, as the reference)")
     p.add_argument("--grad-clip", type=float, default=0.0,
                    help="clip the global gradient norm to this value (0: off; not with the fused DP optimizer)")
     p.add_argument("--seed", type=int, default=1337)
@@ -185,7 +185,8 @@ class Trainer:
             # scatter / all-gather around the native Adam) otherwise. With a
             # single replica the kernel is the bucketed Adam update.
             self.opt = FusedDPAdam(
-                model, self.dp, lr=args.lr, bucket_bytes=int(args.bucket_mb * 1024 * 1024), overlap=self.pipe is None
+                model, self.dp, lr=args.lr, bucket_bytes=int(args.bucket_mb * 1024 * 1024), overlap=self.pipe is None,
+                weight_decay=getattr(args, "weight_decay", 0.0),
             )
         else:
             wd = getattr(args, "weight_decay", 0.0)
@@ -199,9 +200,6 @@ class Trainer:
         if getattr(args, "grad_clip", 0.0) and self.fused_dp:
             raise ValueError("--grad-clip needs the unfused optimizer path (the fused DP optimizer updates "
                              "inside backward); set DST_FUSED_DP=0 or --naive-dp")
-        if getattr(args, "weight_decay", 0.0) and self.fused_dp:
-            raise ValueError("--weight-decay needs the unfused optimizer path (the fused DP optimizer implements "
-                             "plain Adam); set DST_FUSED_DP=0 or --naive-dp")
         self.last_grad_norm = None
         self.reducer = None
         if self.dp.enabled and not args.naive_dp and not self.fused_dp:

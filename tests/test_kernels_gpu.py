@@ -232,6 +232,28 @@ def test_adam_matches_torch():
     assert st["exp_avg"].dtype == torch.float32 and float(st["step"]) == 3
 
 
+def test_adamw_matches_torch():
+    """Decoupled weight decay in the native multi-tensor Adam equals torch.optim.AdamW."""
+    from dstraining_b200.optim.precision import MasterWeightOptimizer
+
+    torch.manual_seed(1)
+    ps = [torch.nn.Parameter(torch.randn(n, device="cuda").to(torch.bfloat16)) for n in (10, 4096, 12345)]
+    opt = MasterWeightOptimizer(ps, lr=1e-3, weight_decay=0.1, decoupled_weight_decay=True)
+    assert opt._native and opt._native_supports()
+    ref_master = [p.detach().float().clone().requires_grad_(True) for p in ps]
+    ref = torch.optim.AdamW(ref_master, lr=1e-3, weight_decay=0.1)
+    for step in range(3):
+        for p, rm in zip(ps, ref_master):
+            g = torch.randn_like(p, dtype=torch.float32).to(torch.bfloat16)
+            p.grad = g
+            rm.grad = g.float()
+        opt.step()
+        ref.step()
+    for p, m, rm in zip(ps, opt.master_params, ref_master):
+        assert (m - rm).abs().max().item() < 1e-6
+        assert torch.equal(p.data, m.to(torch.bfloat16))
+
+
 @pytest.mark.parametrize("B,T,H,D", [(2, 128, 4, 64), (1, 512, 3, 128), (2, 1024, 12, 64), (1, 2048, 2, 128)])
 def test_flash_forward_tcgen05(B, T, H, D):
     """The tcgen05 forward matches the fp32 reference and the mma.sync

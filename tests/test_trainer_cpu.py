@@ -111,3 +111,30 @@ def test_train_profile_window(tmp_path):
         names = [e.get("name") for e in trace["traceEvents"]]
         assert names.count("forward_backward") == 2 and names.count("optimizer") == 2
         assert names.count("block1") == 2
+
+
+def test_fused_dp_adam_weight_decay_is_adamw():
+    """FusedDPAdam's decoupled weight decay (host path; the native kernels
+    apply the same factor) equals torch.optim.AdamW."""
+    import copy
+
+    from dstraining_b200.models.gpt import GPT, GPTConfig
+    from dstraining_b200.optim.fused_dp import FusedDPAdam
+    from dstraining_b200.parallel.topology import SINGLE
+
+    cfg = GPTConfig(vocab_size=128, block_size=16, n_layer=1, n_head=2, n_embd=32)
+    m = GPT(cfg, SINGLE, seed=2)
+    ref = copy.deepcopy(m)
+    opt = FusedDPAdam(m, SINGLE, lr=1e-2, weight_decay=0.3, bucket_bytes=1 << 12)
+    ref_opt = torch.optim.AdamW(ref.parameters(), lr=1e-2, weight_decay=0.3)
+    g = torch.Generator().manual_seed(0)
+    for _ in range(3):
+        x, y = torch.randint(0, 128, (2, 16), generator=g), torch.randint(0, 128, (2, 16), generator=g)
+        opt.zero_grad()
+        m(x, y)[1].backward()
+        opt.step()
+        ref_opt.zero_grad()
+        ref(x, y)[1].backward()
+        ref_opt.step()
+    for (n, p), q in zip(m.named_parameters(), ref.parameters()):
+        assert (p - q).abs().max().item() < 1e-5, n
