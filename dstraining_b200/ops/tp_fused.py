@@ -98,8 +98,17 @@ def ag_gemm(owner, role, tp: TPContext, x_shard2: torch.Tensor, seq: int, w: tor
     shard = _publish_shard(ch, x_shard2)
     tokens = x_shard2.shape[0] * tp.world
     n = w.shape[1] if w_mn else w.shape[0]
+    # Per 128-row block, the kernel counts the 64-column chunks copied into the
+    # gather buffer and waits for epoch * (K / 64): the counters advance only in
+    # launches that cover their block, so they are set to the channel's epoch
+    # whenever the token count changes (stream-ordered after the last launch).
+    kchunks = x_shard2.shape[1] // 64
     if getattr(ch, "arrive", None) is None:
-        ch.arrive = torch.zeros(-(-tokens // 128), dtype=torch.int32, device=x_shard2.device)
+        ch.arrive = torch.full((-(-tokens // 128),), ch.epoch * kchunks, dtype=torch.int32, device=x_shard2.device)
+        ch.arrive_tokens = tokens
+    elif ch.arrive_tokens != tokens:
+        ch.arrive.fill_(ch.epoch * kchunks)
+        ch.arrive_tokens = tokens
     gathered = torch.empty(tokens, x_shard2.shape[1], dtype=x_shard2.dtype, device=x_shard2.device)
     res = native.lib().tp_gemm(
         shard, False, w, w_mn, tokens, n, x_shard2.shape[1], epi, MODE_GATHER_A, ch.buf.ptrs, ch.flags.ptrs, ch.done,
