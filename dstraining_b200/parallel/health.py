@@ -25,6 +25,7 @@ The reference has no failure handling (its only guard is
 
 from __future__ import annotations
 
+import contextlib
 import datetime
 import os
 import signal
@@ -60,6 +61,7 @@ class Heartbeat:
         self.interval = interval
         self.rank = dist.get_rank()
         self.last = time.time()
+        self._held = 0
         self._stop = threading.Event()
         self._thread = threading.Thread(target=self._run, name="dst-heartbeat", daemon=True)
         self.beat()
@@ -67,8 +69,20 @@ class Heartbeat:
     def tick(self) -> None:
         self.last = time.time()
 
+    @contextlib.contextmanager
+    def hold(self):
+        """A long phase that is not a training step (a checkpoint write, an
+        evaluation): while it runs the published time keeps moving, so peers
+        do not take the rank for hung; progress is ticked when it ends."""
+        self._held += 1
+        try:
+            yield
+        finally:
+            self._held -= 1
+            self.tick()
+
     def beat(self) -> None:
-        _store().set(f"{_PREFIX}/hb/{self.rank}", repr(self.last))
+        _store().set(f"{_PREFIX}/hb/{self.rank}", repr(time.time() if self._held else self.last))
 
     def _run(self) -> None:
         while not self._stop.wait(self.interval):

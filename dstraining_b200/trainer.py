@@ -229,6 +229,13 @@ class Trainer:
             hb_timeout = args.heartbeat_timeout
             self.heartbeat, self.watchdog = start_monitoring(interval=min(1.0, hb_timeout / 4), timeout=hb_timeout)
 
+    def hold(self):
+        """Context for a long phase between steps (checkpoint, evaluation): the
+        heartbeat keeps publishing meanwhile (no-op without ``--heartbeat-timeout``)."""
+        import contextlib
+
+        return self.heartbeat.hold() if self.heartbeat is not None else contextlib.nullcontext()
+
     @property
     def n_params(self) -> int:
         return sum(p.numel() for p in self.model.parameters())

@@ -42,6 +42,19 @@ def test_stale_and_failed_ranks(one_rank):
     assert health.stale_ranks(5.0) == [0, 1]  # rank 0 reported a failure
 
 
+def test_hold_keeps_a_busy_rank_fresh(one_rank):
+    """A rank inside a long non-step phase (checkpoint, evaluation) publishes
+    the current time, not its last step; its last step counts again after."""
+    hb = health.Heartbeat(interval=10.0)
+    hb.last -= 100.0
+    with hb.hold():
+        hb.beat()
+        assert 0 not in health.stale_ranks(5.0)
+    hb.last -= 100.0  # the phase has ended: no further steps
+    hb.beat()
+    assert 0 in health.stale_ranks(5.0)
+
+
 def test_step_gate_raises_on_missing_rank(one_rank):
     gate = health.StepGate(timeout=0.3)
     t0 = time.time()

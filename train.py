@@ -159,7 +159,8 @@ def run(args):
                     sink.flush()
                 t_last, s_last = now, step + 1
         if args.eval_every and ((step + 1) % args.eval_every == 0 or last):
-            ev = tr.eval_loss(args.eval_batches)  # every rank takes part
+            with tr.hold():
+                ev = tr.eval_loss(args.eval_batches)  # every rank takes part
             if tr.is_logger:
                 print(f"eval step {step:5d}  loss {ev:.4f}", flush=True)
                 if sink:
@@ -170,10 +171,11 @@ def run(args):
             if args.time_limit_min and time.time() - t_start > args.time_limit_min * 60:
                 stop.flag = True
             if ((step + 1) % max(1, args.signal_check_every) == 0 or last) and stop.agreed(tr.device):
-                if pending is not None:
-                    pending.wait()
-                path = checkpoint.save(args.ckpt_dir, step + 1, tr.model, tr.opt, tr.tp, tr.pp, tr.dp, tr.config,
-                                       args.seed)
+                with tr.hold():
+                    if pending is not None:
+                        pending.wait()
+                    path = checkpoint.save(args.ckpt_dir, step + 1, tr.model, tr.opt, tr.tp, tr.pp, tr.dp,
+                                           tr.config, args.seed)
                 prune(args)
                 if tr.is_logger:
                     print(f"stop requested (signal or time limit): saved {path} after step {step}; exiting",
@@ -187,11 +189,12 @@ def run(args):
                     dist.destroy_process_group()
                 sys.exit(0)
         if args.ckpt_dir and args.ckpt_every and (step + 1) % args.ckpt_every == 0 and not last:
-            if pending is not None:
-                pending.wait()  # one background write at a time
-                prune(args)
-            out = checkpoint.save(args.ckpt_dir, step + 1, tr.model, tr.opt, tr.tp, tr.pp, tr.dp, tr.config,
-                                  args.seed, background=args.ckpt_async)
+            with tr.hold():
+                if pending is not None:
+                    pending.wait()  # one background write at a time
+                    prune(args)
+                out = checkpoint.save(args.ckpt_dir, step + 1, tr.model, tr.opt, tr.tp, tr.pp, tr.dp, tr.config,
+                                      args.seed, background=args.ckpt_async)
             pending = out if args.ckpt_async else None
             if pending is None:
                 prune(args)
@@ -200,11 +203,12 @@ def run(args):
     if args.bench:
         report_bench(args, tr, window, bench_mark(cuda) if window is not None else None, args.steps - first_timed,
                      sink)
-    if pending is not None:
-        pending.wait()
-    if args.ckpt_dir:
-        checkpoint.save(args.ckpt_dir, args.steps, tr.model, tr.opt, tr.tp, tr.pp, tr.dp, tr.config, args.seed)
-        prune(args)
+    with tr.hold():
+        if pending is not None:
+            pending.wait()
+        if args.ckpt_dir:
+            checkpoint.save(args.ckpt_dir, args.steps, tr.model, tr.opt, tr.tp, tr.pp, tr.dp, tr.config, args.seed)
+            prune(args)
     if sink:
         sink.close()
     if dist.is_initialized():
