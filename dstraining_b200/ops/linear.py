@@ -16,6 +16,8 @@ transfer with the GEMM tiles; the unfused NCCL versions in
 
 from __future__ import annotations
 
+import os
+
 from typing import Optional
 
 import torch
@@ -201,6 +203,14 @@ def mlp(x, c_fc, c_proj, residual: Optional[torch.Tensor]):
         and tp_fused.usable(tp, x.shape[1] * tp.world)
     ):
         return tp_fused.mlp_sequence_parallel(x, c_fc.weight, c_fc.bias, c_proj.weight, c_proj.bias, residual, tp)
+    if (
+        os.environ.get("DST_FUSED_TP_MLP", "0") == "1"  # not yet run on GPUs: off by default
+        and c_fc.input_mode == "replicated"
+        and c_proj.output_mode == "replicated"
+        and x.dim() == 3
+        and tp_fused.usable(tp, x.shape[1])
+    ):
+        return tp_fused.mlp_replicated(x, c_fc.weight, c_fc.bias, c_proj.weight, c_proj.bias, residual, tp)
     return _MLPFn.apply(
         x, c_fc.weight, c_fc.bias, c_proj.weight, c_proj.bias, residual, c_fc.tp, c_fc.input_mode, c_proj.output_mode
     )

@@ -256,6 +256,50 @@ class _MLPTP(torch.autograd.Function):
         return dx, dw1, db1, dw2, db2, dres, None
 
 
+class _MLPTPReplicated(torch.autograd.Function):
+    """c_proj(gelu(c_fc(x))) + residual under TP without sequence parallelism
+    (activations replicated): c_fc with its bias + GELU epilogue needs no
+    communication; c_proj's all-reduce (f̄) is the scatter GEMM + ordered slot
+    reduction (bias, residual) + peer all-gather of the reduced rows. Backward:
+    dGELU in the epilogue of the local c_proj dX GEMM, and c_fc's dX all-reduce
+    (f's backward) as scatter GEMM + reduction + all-gather."""
+
+    @staticmethod
+    def forward(ctx, x, w1, b1, w2, b2, residual, tp):
+        B, T = x.shape[0], x.shape[1]
+        x2 = _flat(x.contiguous())
+        pre = torch.empty(x2.shape[0], w1.shape[0], dtype=x2.dtype, device=x2.device)
+        h = gemm(x2, False, w1, False, EPI_BIAS_GELU, bias=b1, aux_out=pre)
+        r2 = None
+        if residual is not None:
+            tl = T // tp.world
+            r2 = _flat(residual[:, tp.rank * tl : (tp.rank + 1) * tl].contiguous())
+        shard = gemm_rs(id(w2), "mlp.rep.proj.rs", tp, h, T, w2, False, bias=b2, resid2=r2)
+        y = allgather_rows(id(w2), "mlp.rep.proj.ag", tp, shard, T).view(B, T, w2.shape[0])
+        ctx.save_for_backward(x2, w1, pre, h, w2)
+        ctx.meta = (tp, T, b1 is not None, b2 is not None, residual is not None, x.shape, id(w1))
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, w1, pre, h, w2 = ctx.saved_tensors
+        tp, T, has_b1, has_b2, has_res, xshape, k1 = ctx.meta
+        dres = dy if has_res else None
+        dy2 = _flat(dy.contiguous())
+        db2 = bias_grad(dy2) if has_b2 else None  # dy is replicated: complete on every rank
+        dpre = gemm(dy2, False, w2, True, EPI_DGELU, aux=pre)
+        dw2 = weight_grad(dy2, h)
+        dx_shard = gemm_rs(k1, "mlp.rep.fc.bwd.rs", tp, dpre, T, w1, True)
+        dx = allgather_rows(k1, "mlp.rep.fc.bwd.ag", tp, dx_shard, T).view(xshape)
+        dw1 = weight_grad(dpre, x2)
+        db1 = bias_grad(dpre) if has_b1 else None
+        return dx, dw1, db1, dw2, db2, dres, None
+
+
+def mlp_replicated(x, w1, b1, w2, b2, residual, tp):
+    return _MLPTPReplicated.apply(x, w1, b1, w2, b2, residual, tp)
+
+
 def column_parallel(x, w, b, tp, mode):
     return _ColumnTP.apply(x, w, b, tp, mode)
 

@@ -1,7 +1,7 @@
 """Fused tensor-parallel kernels (AG+GEMM, GEMM+RS over NVLink) vs tp=1.
 
     torchrun --nproc-per-node 2 tests/suites/tp_fused_suite.py --sp
-    torchrun --nproc-per-node 2 tests/suites/tp_fused_suite.py
+    torchrun --nproc-per-node 2 tests/suites/tp_fused_suite.py [--fused-mlp]
 
 bf16 on CUDA. Every rank builds the TP model and the single-GPU model with
 identical weights (decomposition-invariant init). Checks: the loss matches;
@@ -31,7 +31,13 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--sp", action="store_true")
     ap.add_argument("--device", default="cuda")
+    ap.add_argument("--fused-mlp", action="store_true",
+                    help="without --sp: the fused replicated-activation MLP (DST_FUSED_TP_MLP=1)")
     a = ap.parse_args()
+    if a.fused_mlp:
+        import os
+
+        os.environ["DST_FUSED_TP_MLP"] = "1"
     device = start(a.device)
     tp = topology.make_tp_context()
     rep = Report()
