@@ -50,3 +50,9 @@ def test_gpt2_preset():
     assert out["valid"] and out["per_stage"][0]["params"] == 50257 * 768 + 1024 * 768 + 12 * (12 * 768 * 768 + 13 * 768) \
         + 2 * 768 + 50304 * 768
     assert out["tokens_per_step"] == 16 * 1024
+
+
+def test_plain_tp_mlp_warning():
+    out = plan(parse_args(["--layers", "4", "--heads", "4", "--embd", "256", "--block", "256", "--vocab", "300",
+                           "--tp", "2", "--bf16"]))
+    assert out["valid"] and any("without --sp" in w for w in out["fast_path_warnings"])
