@@ -8,16 +8,18 @@
 optionally from the ``top_k`` most probable and / or the nucleus of
 probability ``top_p``.
 
-* With ``use_cache=True`` (the default; single-process models) the prompt is
-  run once and every later token costs one row per layer: its key and value
-  are appended to a per-layer cache and its query attends over the cache.
+* With ``use_cache=True`` (the default) the prompt is run once and every
+  later token costs one row per layer: its key and value are appended to a
+  per-layer cache and its query attends over the cache (under tensor
+  parallelism each rank caches its own heads; every rank of the group must
+  call it with the same inputs and generator state).
   Positions are learned and absolute, so once the sequence outgrows
   ``block_size`` the window slides and every step re-runs the whole window,
   exactly as without a cache. Runs on the model's own parameters with
   PyTorch ops (fp32 on CPU, the model's dtype on CUDA).
-* Otherwise (and for tensor-parallel models) every step runs the model's
-  full-context forward pass on the last ``block_size`` tokens, right-padded
-  to a multiple of ``pad_to`` so the native causal attention kernels (which
+* Otherwise every step runs the model's full-context forward pass on the
+  last ``block_size`` tokens, right-padded to a multiple of ``pad_to`` so the
+  native causal attention kernels (which
   take sequence lengths in multiples of 64 / 128) can run it - under causal
   attention the padding never influences the positions before it. Every TP
   rank must call it with the same inputs and generator state; pipeline
@@ -35,23 +37,29 @@ import os
 from typing import Optional
 
 import torch
+import torch.distributed as dist
 import torch.nn.functional as F
 
 from ..models.gpt import GPT, GPTConfig
+from ..parallel.comm import all_gather_dim
 from ..parallel.topology import SINGLE
 
 
 class KVCache:
     """Keys and values of every layer for the tokens seen so far, in
     preallocated ``[B, H, block_size, D]`` buffers, and the decoding step of
-    a single-process :class:`GPT` over them (PyTorch ops on the model's
-    parameters)."""
+    a :class:`GPT` over them (PyTorch ops on the model's parameters). Under
+    tensor parallelism each rank caches its own heads; the row-parallel
+    outputs are summed over the group (bias added once, after the sum) and the
+    vocabulary-sharded logits gathered, so every rank sees the same logits -
+    every rank of the group must make the same calls."""
 
     def __init__(self, model: GPT, batch: int):
         cfg = model.config
         self.model = model
+        self.tp = model.tp
         p = model.wte.weight
-        self.H, self.D = cfg.n_head, cfg.n_embd // cfg.n_head
+        self.H, self.D = cfg.n_head // self.tp.world, cfg.n_embd // cfg.n_head
         shape = (batch, self.H, cfg.block_size, self.D)
         self.k = [torch.empty(shape, dtype=p.dtype, device=p.device) for _ in range(cfg.n_layer)]
         self.v = [torch.empty(shape, dtype=p.dtype, device=p.device) for _ in range(cfg.n_layer)]
@@ -60,6 +68,13 @@ class KVCache:
     @staticmethod
     def _ln(ln, x):
         return F.layer_norm(x, ln.normalized_shape, ln.weight, ln.bias, ln.eps)
+
+    def _row(self, x: torch.Tensor, layer) -> torch.Tensor:
+        """Row-parallel linear: local partial product, sum over the group, then the full bias."""
+        y = F.linear(x, layer.weight)
+        if self.tp.enabled:
+            dist.all_reduce(y, group=self.tp.group)
+        return y + layer.bias if layer.bias is not None else y
 
     def forward(self, tokens: torch.Tensor) -> torch.Tensor:
         """Run ``tokens`` [B, t] at positions ``len .. len + t - 1`` (the whole
@@ -81,13 +96,16 @@ class KVCache:
             keys, vals = self.k[i][:, :, : p0 + t], self.v[i][:, :, : p0 + t]
             # the window's first pass is causal; a single new token sees every cached one
             y = F.scaled_dot_product_attention(q, keys, vals, is_causal=p0 == 0 and t > 1)
-            y = y.transpose(1, 2).reshape(b, t, cfg.n_embd)
-            x = x + F.linear(y, a.proj.weight, a.proj.bias)
+            y = y.transpose(1, 2).reshape(b, t, self.H * self.D)
+            x = x + self._row(y, a.proj)
             h = F.gelu(F.linear(self._ln(blk.ln_2, x), blk.mlp.c_fc.weight, blk.mlp.c_fc.bias), approximate="tanh")
-            x = x + F.linear(h, blk.mlp.c_proj.weight, blk.mlp.c_proj.bias)
+            x = x + self._row(h, blk.mlp.c_proj)
         self.len = p0 + t
         x = self._ln(m.ln_f, x[:, -1])
-        return F.linear(x, m.lm_head.weight)[:, : cfg.vocab_size]
+        logits = F.linear(x, m.lm_head.weight)  # this rank's vocabulary shard
+        if self.tp.enabled:
+            logits = all_gather_dim(logits, self.tp, 1)
+        return logits[:, : cfg.vocab_size]
 
 
 def _sample(logits: torch.Tensor, temperature: float, top_k: Optional[int], generator,
@@ -126,7 +144,7 @@ def generate(model: GPT, idx: torch.Tensor, max_new_tokens: int, temperature: fl
              top_k: Optional[int] = None, generator: Optional[torch.Generator] = None, pad_to: int = 128,
              use_cache: bool = True, top_p: Optional[float] = None) -> torch.Tensor:
     cfg = model.config
-    cache = KVCache(model, idx.shape[0]) if (use_cache and not model.tp.enabled) else None
+    cache = KVCache(model, idx.shape[0]) if use_cache else None
     was_training = model.training
     model.eval()
     try:

@@ -68,3 +68,11 @@ def test_top_p_keeps_the_nucleus():
     assert draws == {0, 1}  # 0.5 + 0.3 covers 0.7; tokens 2 and 3 are cut
     draws = {int(_sample(logits, 1.0, None, g, top_p=0.1)) for _ in range(50)}
     assert draws == {0}  # always at least the most probable token
+
+
+def test_kv_cache_tensor_parallel():
+    """tp=2 (gloo): the cached decoder gives the tp=1 logits and tokens."""
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="1")
+    assert launch(2, [os.path.join(root, "tests", "suites", "kv_tp_suite.py"), "--device", "cpu"], timeout=300,
+                  env=env) == 0
