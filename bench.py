@@ -138,7 +138,7 @@ def parallelism_name(lay: dict) -> str:
 
 class ClockSampler:
     """Samples SM clocks / throttle reasons of the visible GPUs with
-    nvidia-smi every 200 ms while active."""
+    nvidia-smi every 50 ms while active."""
 
     def __init__(self):
         self.samples = []
@@ -149,7 +149,7 @@ class ClockSampler:
         q = "index,clocks.sm,clocks.max.sm,power.draw," + ",".join(f"clocks_event_reasons.{r}" for r in REASONS)
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "200"],
+                ["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE,
                 stderr=subprocess.DEVNULL,
                 text=True,
@@ -326,10 +326,10 @@ def run_ours(a, cfg: BenchConfig, lay: dict, rank, world):
         status=status,
         n_params=tr.n_params,
         note=None,
-        optimizer=("Adam on fp32 masters, bf16 params; " + (
-            "DP reduction + update fused in one NVLink kernel per bucket" if getattr(tr.opt, "transport", "") == "peer"
+        impl_detail=(
+            "DP reduction + Adam update fused in one NVLink kernel per bucket" if getattr(tr.opt, "transport", "") == "peer"
             else "NCCL reduce-scatter + sharded Adam + all-gather per bucket" if tr.fused_dp
-            else "NCCL bucketed all-reduce")),
+            else "NCCL bucketed all-reduce" if lay["dp"] > 1 else "native multi-tensor Adam"),
     )
 
 
@@ -480,12 +480,12 @@ def main():
             "parallelism": f"dp{world}" if cfg.name == "c2" else parallelism_name(lay),
             "sequence_parallel": cfg.sp and lay["tp"] > 1,
             "recompute": cfg.recompute,
-            "optimizer": res.get("optimizer", "Adam on fp32 masters, bf16 params"),
+            "optimizer": "Adam on fp32 masters, bf16 params",
             "dp_buckets_mb": 25,
             "l2": "no flush: each step streams several GB of weights/optimizer state/activations (>> 126 MB L2)",
-            "params_rank0": res["n_params"],
-            "final_loss": round(res["loss"], 4),
         },
+        "params_rank0": res["n_params"],
+        "final_loss": round(res["loss"], 4),
         "e2e": {
             "value": round(e2e, 1),
             "unit": "tokens/s",
@@ -503,6 +503,8 @@ def main():
         out["fraction_of_measured_sustained_bf16"] = round(per_gpu / peak, 3)
     if res.get("note"):
         out["note"] = res["note"]
+    if res.get("impl_detail"):
+        out["impl_detail"] = res["impl_detail"]
     if res["sampler"] is not None:
         out["clocks"] = res["sampler"].summary()
     if a.impl == "reference":

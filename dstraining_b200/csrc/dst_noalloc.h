@@ -22,7 +22,7 @@ extern "C" {
 // Return codes of dst_layernorm_bwd_noalloc.
 #define DST_NOALLOC_OK 0
 #define DST_NOALLOC_ERR_TOO_LARGE 1   // hidden size above DST_NOALLOC_MAX_HIDDEN
-#define DST_NOALLOC_ERR_BAD_ARG 2     // null pointer, rows < 1, hidden not a multiple of 8
+#define DST_NOALLOC_ERR_BAD_ARG 2     // null or misaligned pointer, rows < 1, hidden not a multiple of 8
 #define DST_NOALLOC_ERR_CUDA 3        // a CUDA call failed (set-up or launch)
 
 // Largest hidden size (last dimension) the fixed scratch array supports.
@@ -39,7 +39,13 @@ extern "C" {
 //   dy, x, dx : [rows, hidden] bf16, row-major, contiguous
 //   w, dw, db : [hidden] bf16
 //   mean, rstd: [rows] fp32 (as saved by the forward pass)
+//   alignment : dy, x, w and dx start on a 16-byte boundary (they are moved
+//               in 16-byte vectors), mean and rstd on 4 bytes, dw and db on 2;
+//               a misaligned pointer returns DST_NOALLOC_ERR_BAD_ARG
 //   stream    : the stream the work is queued on (0 = legacy default stream)
+//
+// Any hidden size from 8 to DST_NOALLOC_MAX_HIDDEN (a multiple of 8) is
+// handled in full.
 //
 // Scratch: a static device array of 2 * DST_NOALLOC_MAX_CTAS *
 // DST_NOALLOC_MAX_HIDDEN floats (9.25 MiB) compiled into the library; every

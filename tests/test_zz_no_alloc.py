@@ -46,7 +46,9 @@ def _rel(a, b):
     return ((a - b).abs().max() / b.abs().max().clamp_min(1e-6)).item()
 
 
-@pytest.mark.parametrize("rows,hidden", [(3000, 768), (517, 2048)])
+# 768 and 1024 take the two-kernel path; 1032 and up the three-kernel path,
+# up to the largest accepted hidden size (DST_NOALLOC_MAX_HIDDEN = 4096).
+@pytest.mark.parametrize("rows,hidden", [(3000, 768), (257, 1024), (300, 1032), (517, 2048), (1000, 3072), (333, 4096)])
 def test_noalloc_matches_allocating_layernorm_bwd(cuda, rows, hidden):
     lib, fn = _entry()
     for call in range(2):  # two calls in a row share the scratch array
@@ -76,3 +78,8 @@ def test_noalloc_rejects_oversized_and_bad_arguments(cuda):
     assert _call(fn, t, t, v, s, s, t, v, v, rows, hidden) == DST_NOALLOC_ERR_TOO_LARGE
     assert _call(fn, t, t, v, s, s, t, v, v, rows, 12) == DST_NOALLOC_ERR_BAD_ARG
     assert _call(fn, t, t, v, s, s, t, v, v, 0, 64) == DST_NOALLOC_ERR_BAD_ARG
+    # dy, x, w and dx must start on a 16-byte boundary: an offset view is
+    # refused instead of faulting inside the kernel.
+    off = t.view(-1)[1:].view(-1)
+    assert _call(fn, off, t, v, s, s, t, v, v, 2, 64) == DST_NOALLOC_ERR_BAD_ARG
+    assert _call(fn, t, t, v, s, s, off, v, v, 2, 64) == DST_NOALLOC_ERR_BAD_ARG
