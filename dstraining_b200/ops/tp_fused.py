@@ -30,6 +30,7 @@ from __future__ import annotations
 from typing import Dict, Tuple
 
 import torch
+import torch.distributed as dist
 
 from ..parallel.symm import PeerBuffer
 from ..parallel.topology import TPContext, peer_reachable
@@ -57,6 +58,27 @@ class _Channel:
     def view(self, numel: int) -> torch.Tensor:
         return self.buf.view(torch.bfloat16)[:numel]
 
+    def retire(self) -> None:
+        """Release this channel's memory safely (collective over the group): a
+        peer's kernel may still be reading or writing this rank's buffers over
+        NVLink, which freeing memory does not wait for, so every rank first
+        finishes its own work on the device, then the group agrees that all
+        have, then each rank unmaps its peers' buffers; the local buffers are
+        freed when the last reference goes."""
+        _quiesce(self.tp, self.buf.device)
+        self.buf.close()
+        self.flags.close()
+
+
+def _quiesce(tp: TPContext, device: torch.device) -> None:
+    """Every rank of ``tp`` has finished all work queued on its device."""
+    if device.type == "cuda":
+        torch.cuda.synchronize(device)
+    if tp.enabled and dist.is_initialized():
+        dist.barrier(group=tp.group)
+        if device.type == "cuda":
+            torch.cuda.synchronize(device)
+
 
 _CHANNELS: Dict[Tuple[int, str, Tuple[int, ...]], _Channel] = {}
 
@@ -65,10 +87,14 @@ def channel(owner: int, role: str, tp: TPContext, nbytes: int, device: torch.dev
     """The channel of one call site, keyed by the owning layer (the id of its
     weight Parameter, captured in forward), a role and the group's ranks (an
     id can be reused by a later model in another group); created or grown
-    collectively in program order."""
+    collectively in program order. A channel that must grow is retired first
+    (every rank's work on it finished, peers' mappings closed)."""
     key = (owner, role, tuple(tp.ranks))
     ch = _CHANNELS.get(key)
     if ch is None or ch.nbytes < nbytes:
+        if ch is not None:
+            del _CHANNELS[key]
+            ch.retire()
         ch = _Channel(tp, device, nbytes)
         _CHANNELS[key] = ch
     return ch

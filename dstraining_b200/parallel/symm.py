@@ -30,6 +30,7 @@ class PeerBuffer:
         lib = native.lib()
         self.ctx = ctx
         self.device = device
+        self._opened: List[int] = []
         self.nbytes = nbytes
         self.local, handle = lib.symm_alloc(int(nbytes), device.index)
         handles: List = [None] * ctx.world

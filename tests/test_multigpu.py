@@ -13,12 +13,22 @@ pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
+def _free_port():
+    """A port nothing listens on now, so several groups of these tests can run
+    side by side on disjoint GPUs (CUDA_VISIBLE_DEVICES) of one machine."""
+    import socket
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
 def _torchrun(n, script, *args, timeout=420):
     if torch.cuda.device_count() < n:
         pytest.skip(f"needs {n} GPUs")
     env = dict(os.environ, DST_PG_TIMEOUT_S="120", NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", str(timeout), sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           f"--nproc-per-node={n}", "--master-addr=127.0.0.1", f"--master-port={29400 + os.getpid() % 500}",
+           f"--nproc-per-node={n}", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
            os.path.join(ROOT, script), *args]
     r = subprocess.run(cmd, env=env, cwd=ROOT, capture_output=True, text=True)
     errors = [ln for ln in r.stderr.splitlines() if "error" in ln.lower() and not ln.startswith("frame #")]
@@ -37,6 +47,27 @@ def test_tp_suite_2gpu_nccl():
 @pytest.mark.parametrize("sp", [True, False])
 def test_tp_fused_2gpu(sp):
     _torchrun(2, "tests/suites/tp_fused_suite.py", *(["--sp"] if sp else []))
+
+
+@pytest.mark.parametrize("n", [4, 8])
+@pytest.mark.parametrize("sp", [True, False])
+def test_tp_fused_wide(n, sp):
+    """The fused AG+GEMM / GEMM+RS kernels at tp=4 and tp=8 (row-block source
+    order, per-block arrival counters and receive slots for more than two
+    ranks)."""
+    _torchrun(n, "tests/suites/tp_fused_suite.py", *(["--sp"] if sp else []))
+
+
+@pytest.mark.parametrize("n", [2, 4])
+def test_tp_fused_replicated_mlp(n):
+    """Plain TP (no SP): the MLP's all-reduces as scatter GEMM + slot reduction
+    + peer all-gather."""
+    _torchrun(n, "tests/suites/tp_fused_suite.py", "--fused-mlp")
+
+
+@pytest.mark.parametrize("n", [4, 8])
+def test_fused_dp_adam_wide(n):
+    _torchrun(n, "tests/suites/fused_dp_suite.py", "--dp", str(n), "--device", "cuda", "--bf16")
 
 
 def test_pp_1f1b_2gpu_nccl():
@@ -72,7 +103,7 @@ def test_step_gate_2gpu(tmp_path):
     marker = str(tmp_path / "g")
     env = dict(os.environ, DST_PG_TIMEOUT_S="120", NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={29400 + os.getpid() % 500}",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
            os.path.join(ROOT, "tests/suites/gate_suite.py"), "--device", "cuda", "--marker", marker]
     r = subprocess.run(cmd, env=env, cwd=ROOT, capture_output=True, text=True)
     print(r.stdout[-3000:], r.stderr[-2000:])
