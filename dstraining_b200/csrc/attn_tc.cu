@@ -69,6 +69,26 @@ __device__ __forceinline__ void store_p_quarter(uint8_t* pbuf, int row, int qtr,
   }
 }
 
+// The whole 128-key row `row` of P into the P tile (four quarters of 32 keys).
+__device__ __forceinline__ void store_p_row(uint8_t* pbuf, int row, const float (&p)[128]) {
+#pragma unroll
+  for (int qtr = 0; qtr < 4; ++qtr) {
+    uint8_t* atom = pbuf + (qtr >> 1) * kAtom + row * 128;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint4 pk;
+      uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(p[qtr * 32 + c * 8 + 2 * j], p[qtr * 32 + c * 8 + 2 * j + 1]);
+        w[j] = *reinterpret_cast<uint32_t*>(&h);
+      }
+      const int c16 = (qtr & 1) * 4 + c;
+      *reinterpret_cast<uint4*>(atom + ((c16 ^ (row & 7)) << 4)) = pk;
+    }
+  }
+}
+
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
@@ -543,26 +563,47 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      const bool diag = (j == nkb - 1);
-      const int kbase = j * 128;
-      float mx = -INFINITY;
+      // The whole 128-key row of S_j in registers: one TMEM read per block.
+      float v[128];
+      tmem_ld128_sync(tS, v);
+      if (j == nkb - 1) {  // diagonal block (warp-uniform): keys after the query are masked
+        const int kbase = j * 128;
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        float v[64];
-        tmem_ld64_sync(tS + hh * 64, v);
-#pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          const bool masked = diag && (kbase + hh * 64 + i > q);
-          mx = fmaxf(mx, masked ? -INFINITY : v[i]);
-        }
+        for (int i = 0; i < 128; ++i)
+          if (kbase + i > q) v[i] = -INFINITY;
       }
-      const float m_blk = mx * scale_log2;
+      float mx4[4] = {v[0], v[1], v[2], v[3]};
+#pragma unroll
+      for (int i = 4; i < 128; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], v[i]);
+      const float m_blk = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * scale_log2;
       const bool need = m_blk > m_ref + 8.f;  // this row's reference maximum moves
       const float c = need ? exp2f(m_ref - m_blk) : 1.f;
       if (need) {
         l *= c;
         m_ref = m_blk;
       }
+      // P = exp2(s * scale - m_ref), packed to bf16 pairs as it is made (the
+      // fp32 scores die as the packed row grows), then into the P tile.
+      uint32_t pk[64];
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const float p0 = exp2f(fmaf(v[2 * i], scale_log2, -m_ref));
+        const float p1 = exp2f(fmaf(v[2 * i + 1], scale_log2, -m_ref));
+        rs4[i & 3] += p0 + p1;
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
+        pk[i] = *reinterpret_cast<uint32_t*>(&h2);
+      }
+#pragma unroll
+      for (int c16 = 0; c16 < 16; ++c16) {  // 16-byte chunk c16 of the row: keys 8*c16 .. +7
+        uint8_t* atom = pbuf + (c16 >> 3) * kAtom + r * 128;
+        *reinterpret_cast<uint4*>(atom + (((c16 & 7) ^ (r & 7)) << 4)) =
+            make_uint4(pk[4 * c16], pk[4 * c16 + 1], pk[4 * c16 + 2], pk[4 * c16 + 3]);
+      }
+      const float rowsum = (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
+      // O rescale (rare once the reference maxima settle); PV_{j-1} has
+      // completed (covered by the commit of S_j), PV_j is issued only after
+      // this thread arrives on p_full below.
       if (j > 0 && __any_sync(0xffffffff, need)) {  // whole warp; other rows scale by 1
 #pragma unroll 1
         for (int ch = 0; ch < D / 32; ++ch) {
@@ -572,20 +613,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 32; ++i) o[i] *= c;
           tmem_st32_sync(tO + ch * 32, o);
         }
-      }
-      float rowsum = 0.f;
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        float v[64];
-        tmem_ld64_sync(tS + hh * 64, v);
-#pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          const bool masked = diag && (kbase + hh * 64 + i > q);
-          v[i] = masked ? 0.f : exp2f(v[i] * scale_log2 - m_ref);
-          rowsum += v[i];
-        }
-        store_p_quarter(pbuf, r, hh * 2, *reinterpret_cast<const float(*)[32]>(v));
-        store_p_quarter(pbuf, r, hh * 2 + 1, *reinterpret_cast<const float(*)[32]>(v + 32));
       }
       l += rowsum;
       tc_fence_before();

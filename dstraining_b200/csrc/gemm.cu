@@ -150,6 +150,9 @@ void gemm_run(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, in
     TORCH_CHECK(p.out != nullptr, "gemm: missing output");
     to = make_tmap_bf16(p.out, N, M, p.ldo, kEpiChunk, 32);
     if (epi == kEpiBiasGelu) tx = make_tmap_bf16(p.aux_out, N, M, p.ldo, kEpiChunk, 32);
+    // residual / pre-activation operand: prefetched into L2 by the producer
+    if ((epi == kEpiBiasResid || epi == kEpiDGelu) && p.aux != nullptr)
+      tx = make_tmap_bf16(p.aux, N, M, p.ld_aux, kEpiChunk, 32);
   }
   if (BN == 256)
     dispatch_layout<256>(a_mn, b_mn, epi, ta, tb, to, tx, p, grid, st);
@@ -373,7 +376,7 @@ static void peer_dispatch(int epi, const CUtensorMap& ta, const CUtensorMap& tb,
   } else if constexpr (MODE == 1 && !A_MN && B_MN) {
     switch (epi) {
       case kEpiStore: return launch_one<BN, A_MN, B_MN, kEpiStore, G, SC>(ta, tb, to, ta, p, grid, st, &pa);
-      case kEpiDGelu: return launch_one<BN, A_MN, B_MN, kEpiDGelu, G, SC>(ta, tb, to, ta, p, grid, st, &pa);
+      case kEpiDGelu: return launch_one<BN, A_MN, B_MN, kEpiDGelu, G, SC>(ta, tb, to, tx, p, grid, st, &pa);
       default: break;
     }
   } else if constexpr ((MODE == 1 || MODE == 2) && A_MN && B_MN) {
@@ -524,6 +527,8 @@ std::vector<at::Tensor> tp_gemm(const at::Tensor& A, bool a_mn, const at::Tensor
   p.status = status_ptr();
   CUtensorMap to = ta, tx = ta;
   if (mode != 3 && epi != kEpiPartialF32) to = make_tmap_bf16(p.out, N, M, N, kEpiChunk, 32);
+  if ((epi == kEpiBiasResid || epi == kEpiDGelu) && p.aux != nullptr)
+    tx = make_tmap_bf16(p.aux, N, M, p.ld_aux, kEpiChunk, 32);
   if (epi == kEpiBiasGelu) {
     p.aux_out = reinterpret_cast<__nv_bfloat16*>(pre.data_ptr());
     tx = make_tmap_bf16(pre.data_ptr(), N, M, N, kEpiChunk, 32);

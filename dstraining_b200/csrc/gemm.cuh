@@ -306,6 +306,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int n0 = nb_ * BN;
         const int kb0 = split * p.k_blocks_per_split;
         const int kb1 = min(kb0 + p.k_blocks_per_split, k_blocks_total);
+        if (EPI == kEpiBiasResid || EPI == kEpiDGelu) {
+          // The epilogue reads this tile's auxiliary operand (residual /
+          // pre-activation) a mainloop later: bring it into L2 now.
+#pragma unroll 1
+          for (int r = 0; r < kBM; r += 32)
+#pragma unroll 1
+            for (int c = 0; c < BN; c += kEpiChunk) tma_prefetch_l2_2d(&tmAux, n0 + c, m0 + r);
+        }
         const CUtensorMap* rowA = &tmA;
         int row_a = m0;
         if (kRowGather) {

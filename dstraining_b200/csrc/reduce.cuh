@@ -1,11 +1,13 @@
 // Deterministic column reductions of row-major matrices.
 //
-// Pass 1 (colred_stage1): CTA (x, y) owns 256 columns and a block of rows;
-// each of its 8 warps walks every 8th row of the block with one 16-byte load
-// (8 columns) per lane, accumulating in fp32 registers; the warps are then
-// combined through shared memory in warp order and the CTA writes one fp32
-// partial row. Optional per-row transform for LayerNorm's dγ: the value
-// summed is dy * (x - mean) * rstd, and a second output receives Σ dy.
+// Pass 1 (colred_stage1): CTA (x, y) owns 256 columns and a block of 64
+// rows; each of its 8 warps walks every 8th row of the block with one
+// 16-byte load (8 columns) per lane, four rows' loads issued before any is
+// used (enough bytes in flight to keep HBM busy), accumulating in fp32
+// registers in row order; the warps are then combined through shared memory
+// in warp order and the CTA writes one fp32 partial row. Optional per-row
+// transform for LayerNorm's dγ: the value summed is dy * (x - mean) * rstd,
+// and a second output receives Σ dy.
 //
 // Pass 2 (colred_stage2): each CTA owns 32 columns of the [R, C] partials;
 // warp w sums rows w, w+8, ... in order, then warp 0 adds the 8 warp sums in
@@ -17,7 +19,7 @@
 
 namespace dst {
 
-constexpr int kColredRows = 128;  // rows per pass-1 CTA
+constexpr int kColredRows = 64;  // rows per pass-1 CTA
 
 __device__ __forceinline__ void colred_unpack(const uint4& u, float (&f)[8]) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
@@ -44,21 +46,40 @@ static __global__ void __launch_bounds__(256) colred_stage1(const __nv_bfloat16*
   const int r1 = min(rows, r0 + kColredRows);
   float s0[8] = {0, 0, 0, 0, 0, 0, 0, 0}, s1[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   if (col < C) {
-    for (int r = r0 + warp; r < r1; r += 8) {
-      float av[8];
-      colred_unpack(*reinterpret_cast<const uint4*>(a + static_cast<size_t>(r) * C + col), av);
-      if (LN) {
-        float xv[8];
-        colred_unpack(*reinterpret_cast<const uint4*>(x + static_cast<size_t>(r) * C + col), xv);
-        const float mu = mean[r], rs = rstd[r];
+    constexpr int U = 4;  // rows in flight per warp
+    for (int rb = r0 + warp; rb < r1; rb += 8 * U) {
+      uint4 ap[U], xp[U];
+      float mu[U], rs[U];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          s0[j] += av[j] * (xv[j] - mu) * rs;
-          s1[j] += av[j];
+      for (int u = 0; u < U; ++u) {
+        const int r = rb + 8 * u;
+        if (r < r1) {
+          ap[u] = __ldg(reinterpret_cast<const uint4*>(a + static_cast<size_t>(r) * C + col));
+          if (LN) {
+            xp[u] = __ldg(reinterpret_cast<const uint4*>(x + static_cast<size_t>(r) * C + col));
+            mu[u] = mean[r];
+            rs[u] = rstd[r];
+          }
         }
-      } else {
+      }
 #pragma unroll
-        for (int j = 0; j < 8; ++j) s0[j] += av[j];
+      for (int u = 0; u < U; ++u) {
+        if (rb + 8 * u < r1) {
+          float av[8];
+          colred_unpack(ap[u], av);
+          if (LN) {
+            float xv[8];
+            colred_unpack(xp[u], xv);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              s0[j] += av[j] * (xv[j] - mu[u]) * rs[u];
+              s1[j] += av[j];
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) s0[j] += av[j];
+          }
+        }
       }
     }
   }

@@ -5,7 +5,8 @@ tile reduces its fp32 accumulator rows to (max, sum exp) and picks the target
 logit when the target id falls inside the tile, so the loss needs no pass
 over the logits. Per-tile stats merge in tile order into per-row stats; under
 TP the ``[3, N]`` per-rank stats are all-gathered and merged in rank order
-(one collective; bitwise identical on every rank).
+(bitwise identical on every rank): by one peer-memory gather kernel over
+NVLink when the group's GPUs can address each other, else one collective.
 
 With sequence parallelism the head's input arrives sequence-sharded: the GEMM
 gathers it from the peers itself (gather mode of ``tp_gemm``), the dX of the
@@ -53,7 +54,15 @@ class _FusedHeadCE(torch.autograd.Function):
         m, s = lib.ce_merge_tiles(tmax, tsum, tg, real_vocab)  # also flags target ids outside the vocabulary
         stats = torch.stack([m, s, tgt])[None]
         if tp.enabled:
-            stats = all_gather_dim(stats, tp, 0)
+            n_rows = stats.shape[-1]
+            if tp_fused.usable(tp, seq) and n_rows % 4 == 0:
+                # Peer-memory gather of every rank's [3, N] fp32 stats (moved as
+                # bytes: [3, 2N] bf16 rows, concatenated in rank order).
+                flat = stats.view(3, n_rows).view(torch.bfloat16)
+                stats = tp_fused.allgather_rows(id(w), "head.stats", tp, flat, 3 * tp.world)
+                stats = stats.view(torch.float32).view(tp.world, 3, n_rows)
+            else:
+                stats = all_gather_dim(stats, tp, 0)
         lse, tgt_all = merge_stats(stats)
         loss = (lse - tgt_all).mean()
         ctx.save_for_backward(logits, lse, x2, w, tg)

@@ -105,6 +105,22 @@ class _Bucket:
         elif g.data_ptr() != dst.data_ptr():
             dst.copy_(g)
 
+    def stage_all(self) -> None:
+        """Copy every parameter's gradient into the bucket's gradient buffer
+        with one multi-tensor copy (a handful of kernels instead of one copy
+        per parameter)."""
+        dsts, srcs = [], []
+        for i, p in enumerate(self.params):
+            g = p.grad
+            dst = self.slot(i)
+            if g is None:
+                dst.zero_()
+            elif g.data_ptr() != dst.data_ptr():
+                dsts.append(dst)
+                srcs.append(g)
+        if dsts:
+            torch._foreach_copy_(dsts, srcs)
+
 
 class FusedDPAdam:
     """DP gradient averaging fused with fp32-master Adam (module docstring):
@@ -188,8 +204,9 @@ class FusedDPAdam:
         b, i = self._where[id(p)]
         if b.late:
             return  # staged in step(), after finalize_grads
-        b.stage(i)
-        b.filled.add(i)
+        if not self.native:
+            b.stage(i)
+        b.filled.add(i)  # on CUDA the bucket is staged in one multi-tensor copy at launch
         self._launch_ready()
 
     def _launch_ready(self) -> None:
@@ -205,6 +222,8 @@ class FusedDPAdam:
             self._step += 1
             self._stepped = True
         b.launched = True
+        if self.native:
+            b.stage_all()
         if self.transport == "peer":
             self._launch_native(b)
         elif self.transport == "collectives":
@@ -305,7 +324,8 @@ class FusedDPAdam:
             if not b.launched:
                 for i in range(len(b.params)):
                     if b.late or i not in b.filled:
-                        b.stage(i)
+                        if not self.native:
+                            b.stage(i)
                         b.filled.add(i)
         self._launch_ready_all()
         if self.native:

@@ -14,7 +14,9 @@ warm-up, synchronised on both sides, max over ranks):
 
 and reports each as a fraction of its roofline: the slower of FLOPs at the
 measured bf16 peak and the bytes each rank must move over NVLink at the
-measured 770 GB/s per direction.
+measured 770 GB/s per direction. Beside each fused kernel's algorithmic
+NVLink bytes it prints the bytes this GPU actually sent and received per
+call, from NVML's NVLink throughput counters (read-only queries).
 """
 
 from __future__ import annotations
@@ -32,6 +34,66 @@ from ..parallel import topology
 from .kernel_bench import peaks
 
 NVLINK_GBS = 770.0
+_NVML_TX, _NVML_RX = 138, 139  # NVML field ids: NVLink data throughput counters (cumulative KiB)
+
+
+class NvlinkCounters:
+    """This GPU's NVLink data bytes sent / received, read from NVML's cumulative
+    throughput counters (read-only queries; nothing is configured). Summed over
+    the links; ``None`` where the driver offers no such counter."""
+
+    def __init__(self, device_index: int):
+        self.h = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            props = torch.cuda.get_device_properties(device_index)
+            try:  # NVML numbers GPUs by PCI address, CUDA may not
+                bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+                self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.links = [ln for ln in range(18) if self._state(ln)]
+        except Exception:  # no NVML or no NVLink: the bench still runs
+            self.h = None
+
+    def _state(self, link):
+        try:
+            return self.nvml.nvmlDeviceGetNvLinkState(self.h, link) == 1
+        except Exception:
+            return False
+
+    def read(self):
+        """(tx_bytes, rx_bytes) so far, or None."""
+        if self.h is None or not self.links:
+            return None
+        try:
+            tx = rx = 0
+            for ln in self.links:
+                vals = self.nvml.nvmlDeviceGetFieldValues(self.h, [(_NVML_TX, ln), (_NVML_RX, ln)])
+                if any(v.nvmlReturn != 0 for v in vals):
+                    return None
+                tx += vals[0].value.ullVal
+                rx += vals[1].value.ullVal
+            return tx * 1024, rx * 1024
+        except Exception:
+            return None
+
+
+def nvlink_bytes_per_call(counters, fn, iters=10):
+    """NVLink bytes this GPU sent and received per call of ``fn`` (counter
+    difference over ``iters`` synchronised calls), or None."""
+    torch.cuda.synchronize()
+    a = counters.read()
+    for _ in range(iters):
+        fn()
+    torch.cuda.synchronize()
+    b = counters.read()
+    if a is None or b is None:
+        return None
+    return {"tx_bytes": (b[0] - a[0]) / iters, "rx_bytes": (b[1] - a[1]) / iters}
 
 
 def timed(fn, iters=10, warmup=3):
@@ -64,6 +126,7 @@ def main():
     dev = torch.device("cuda", torch.cuda.current_device())
     torch.manual_seed(tp.rank)
     tf_peak, _, tag = peaks()
+    counters = NvlinkCounters(torch.cuda.current_device())
     M, C, F = a.tokens, a.hidden, a.ffn // n
     rows = M // n
     bf = torch.bfloat16
@@ -85,7 +148,8 @@ def main():
     roof = max(flops / (tf_peak * 1e12), nv_bytes / (NVLINK_GBS * 1e9)) * 1e3
     t_f, t_n = timed(fused), timed(nccl_ag)
     out["ag_gemm"] = {"fused_ms": t_f, "nccl_gemm_ms": t_n, "roofline_ms": roof, "fraction_of_roofline": roof / t_f,
-                      "speedup_vs_nccl": t_n / t_f}
+                      "speedup_vs_nccl": t_n / t_f, "algorithmic_nvlink_bytes": nv_bytes,
+                      "nvlink_counters": nvlink_bytes_per_call(counters, fused)}
 
     # ---- GEMM + RS: y[M/n, C] = RS(h[M, F] W2[C, F]^T)
     h = torch.randn(M, F, device=dev, dtype=bf)
@@ -105,7 +169,8 @@ def main():
     roof = max(flops / (tf_peak * 1e12), nv_bytes / (NVLINK_GBS * 1e9)) * 1e3
     t_f, t_n = timed(fused_rs), timed(nccl_rs)
     out["gemm_rs"] = {"fused_ms": t_f, "nccl_gemm_ms": t_n, "roofline_ms": roof, "fraction_of_roofline": roof / t_f,
-                      "speedup_vs_nccl": t_n / t_f}
+                      "speedup_vs_nccl": t_n / t_f, "algorithmic_nvlink_bytes": nv_bytes,
+                      "nvlink_counters": nvlink_bytes_per_call(counters, fused_rs)}
 
     # ---- DP bucket: reduce + Adam + all-gather
     from ..optim.fused_dp import FusedDPAdam
@@ -137,7 +202,8 @@ def main():
     roof = nv_bytes / (NVLINK_GBS * 1e9) * 1e3
     t_f, t_n = timed(fused_dp), timed(nccl_dp)
     out["dp_bucket"] = {"bucket_mb": a.bucket_mb, "fused_ms": t_f, "nccl_adam_ms": t_n, "roofline_ms": roof,
-                        "fraction_of_roofline": roof / t_f, "speedup_vs_nccl": t_n / t_f}
+                        "fraction_of_roofline": roof / t_f, "speedup_vs_nccl": t_n / t_f,
+                        "algorithmic_nvlink_bytes": nv_bytes, "nvlink_counters": nvlink_bytes_per_call(counters, fused_dp)}
     out["status"] = int(native.lib().read_status(True))
     out["peak"] = f"bf16 {tf_peak} TFLOP/s {tag}; NVLink {NVLINK_GBS} GB/s per direction (measured copy)"
     if tp.rank == 0:

@@ -6,7 +6,9 @@
 
 Each measurement: ``--warmup`` untimed calls, then ``--iters`` calls each
 timed alone with CUDA events on the launching stream, with a 256 MB buffer
-written between calls so L2 (126 MB) holds nothing useful; reports the mean
+written just before each call so L2 (126 MB) holds nothing useful (that
+write also keeps the GPU busy while the host queues the call, so the host's
+launch work stays outside the interval); reports the mean
 time, achieved TFLOP/s (GEMM, attention) or GB/s (memory-bound kernels), and
 the fraction of the measured peaks in ``MEASURED_PEAKS.json`` (cuBLAS bf16
 burst and copy bandwidth) when that file exists. Used as the small, bounded
@@ -42,9 +44,13 @@ class Timer:
             fn()
         total = 0.0
         for _ in range(iters):
-            self.flush.fill_(1.0)
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             torch.cuda.synchronize()
+            # The flush keeps the GPU busy while the host queues the start
+            # event and the measured call, so the interval holds the kernels'
+            # device time and not the host's launch work (as in a training
+            # step, where launches run ahead of the device).
+            self.flush.fill_(1.0)
             s.record()
             fn()
             e.record()

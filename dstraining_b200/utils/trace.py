@@ -1,5 +1,6 @@
 """Timeline tracing: NVTX ranges (``DST_NVTX=1``) and ``torch.profiler``
-windows (``train.py --profile-dir``).
+windows (``train.py --profile-dir``: a Chrome trace and a per-kernel
+device-time table per rank).
 
 ``nvtx_range(name)`` is a context manager that pushes an NVTX range around
 its body when ``DST_NVTX`` is set and CUDA is available, and marks the same
@@ -84,4 +85,48 @@ class StepProfiler:
         os.makedirs(self.out_dir, exist_ok=True)
         self.path = os.path.join(self.out_dir, f"trace_rank{self.rank}.json")
         self.prof.export_chrome_trace(self.path)
+        if self.cuda:
+            with open(os.path.join(self.out_dir, f"kernels_rank{self.rank}.txt"), "w") as f:
+                f.write(kernel_summary(self.prof, self.end - self.start))
         self.prof = None
+
+
+def kernel_summary(prof, steps: int = 1) -> str:
+    """Device time per kernel name over a recorded window: calls and
+    microseconds per step, share of the summed kernel time, and the device
+    busy fraction (union of kernel intervals over the span from the first
+    kernel's start to the last one's end; below 1 means the GPU waited for the
+    host or for other GPUs)."""
+    rows, spans = {}, []
+    for ev in prof.events():
+        if ev.device_type != torch.autograd.DeviceType.CUDA or getattr(ev, "is_user_annotation", False):
+            continue  # device-side copies of the host's named ranges are not kernels
+        name = ev.name
+        if name.startswith("Memcpy") or name.startswith("Memset"):
+            kind = name.split()[0]
+        else:
+            kind = name
+        dur = ev.time_range.end - ev.time_range.start  # microseconds
+        r = rows.setdefault(kind, [0, 0.0])
+        r[0] += 1
+        r[1] += dur
+        spans.append((ev.time_range.start, ev.time_range.end))
+    if not spans:
+        return "no device activity recorded\n"
+    spans.sort()
+    busy, cur_s, cur_e = 0.0, spans[0][0], spans[0][1]
+    for s0, e0 in spans[1:]:
+        if s0 > cur_e:
+            busy += cur_e - cur_s
+            cur_s, cur_e = s0, e0
+        else:
+            cur_e = max(cur_e, e0)
+    busy += cur_e - cur_s
+    wall = spans[-1][1] - spans[0][0]
+    total = sum(v[1] for v in rows.values())
+    out = [f"window: {steps} step(s); span {wall / steps:.1f} us/step; device busy {busy / steps:.1f} us/step "
+           f"({busy / wall:.1%} of the span); summed kernel time {total / steps:.1f} us/step",
+           f"{'us/step':>10s} {'share':>7s} {'calls/step':>10s}  kernel"]
+    for kind, (n, t) in sorted(rows.items(), key=lambda kv: -kv[1][1]):
+        out.append(f"{t / steps:10.1f} {t / total:7.1%} {n / steps:10.1f}  {kind[:150]}")
+    return "\n".join(out) + "\n"
