@@ -308,6 +308,14 @@ def run_ours(a, cfg: BenchConfig, lay: dict, rank, world):
     ours, other, top_other = (
         count_launches(lambda i: tr.step_device(*dev_batches[0]), ["dst::"]) if not a.no_count else (0, 0, [])
     )
+    dp_timing = None
+    if getattr(tr, "fused_dp", False) and lay["dp"] > 1 and hasattr(tr.opt, "timings"):
+        # one more (untimed) step with per-bucket events on the optimizer's side stream
+        tr.opt.record_timings = True
+        tr.step_device(*dev_batches[0])
+        tr.opt.record_timings = False
+        dp_timing = tr.opt.timings()
+        dp_timing["exposed_ms_max_over_ranks"] = max_over_ranks(dp_timing.get("exposed_ms", 0.0))
     status = None
     from dstraining_b200.ops import native
 
@@ -326,6 +334,7 @@ def run_ours(a, cfg: BenchConfig, lay: dict, rank, world):
         status=status,
         n_params=tr.n_params,
         note=None,
+        dp_timing=dp_timing,
         impl_detail=(
             "DP reduction + Adam update fused in one NVLink kernel per bucket" if getattr(tr.opt, "transport", "") == "peer"
             else "NCCL reduce-scatter + sharded Adam + all-gather per bucket" if tr.fused_dp
@@ -505,6 +514,8 @@ def main():
         out["note"] = res["note"]
     if res.get("impl_detail"):
         out["impl_detail"] = res["impl_detail"]
+    if res.get("dp_timing"):
+        out["dp_bucket_timing"] = res["dp_timing"]
     if res["sampler"] is not None:
         out["clocks"] = res["sampler"].summary()
     if a.impl == "reference":

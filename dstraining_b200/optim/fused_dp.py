@@ -185,6 +185,9 @@ class FusedDPAdam:
             self.done = torch.zeros(1, dtype=torch.int32, device=self.device)
         if self.native:
             self.side = torch.cuda.Stream(device=self.device)
+        self.record_timings = False  # per-bucket CUDA events on the side stream (see timings())
+        self._events = []
+        self._tail = None
         if overlap:
             for p in order:
                 p.register_post_accumulate_grad_hook(self._hook)
@@ -224,12 +227,20 @@ class FusedDPAdam:
         b.launched = True
         if self.native:
             b.stage_all()
+        timed = self.record_timings and self.native
+        if timed:
+            ev_stage = torch.cuda.Event(enable_timing=True)
+            ev_stage.record(torch.cuda.current_stream(self.device))
         if self.transport == "peer":
             self._launch_native(b)
         elif self.transport == "collectives":
             self._launch_sharded(b)
         else:
             self._launch_emulated(b)
+        if timed:
+            ev_done = torch.cuda.Event(enable_timing=True)
+            ev_done.record(self.side)
+            self._events.append((self.buckets.index(b), b.numel, ev_stage, ev_done))
 
     def _launch_native(self, b: _Bucket) -> None:
         self.epoch += 1
@@ -329,6 +340,12 @@ class FusedDPAdam:
                         b.filled.add(i)
         self._launch_ready_all()
         if self.native:
+            if self.record_timings:
+                ev_main = torch.cuda.Event(enable_timing=True)
+                ev_main.record(torch.cuda.current_stream(self.device))
+                ev_side = torch.cuda.Event(enable_timing=True)
+                ev_side.record(self.side)
+                self._tail = (ev_main, ev_side)
             torch.cuda.current_stream(self.device).wait_stream(self.side)
         for b in self.buckets:
             b.filled = set()
@@ -340,6 +357,25 @@ class FusedDPAdam:
         while self._next < len(self.buckets):
             self._launch(self.buckets[self._next])
             self._next += 1
+
+    # -- timing -------------------------------------------------------------
+    def timings(self) -> dict:
+        """Per-bucket timing of the last step run with ``record_timings`` set
+        (synchronises the device): for every bucket, the milliseconds from its
+        gradients being staged on the compute stream to its update finishing on
+        the side stream, and ``exposed_ms``, how long the compute stream's last
+        work of the step ran before the side stream finished (the DP time that
+        backward did not hide; 0 or less when it was hidden). Clears the record."""
+        if not self._events:
+            return {}
+        torch.cuda.synchronize(self.device)
+        rows = [{"bucket": i, "numel": n, "stage_to_done_ms": round(a.elapsed_time(b), 4)}
+                for i, n, a, b in self._events]
+        out = {"buckets": rows}
+        if self._tail is not None:
+            out["exposed_ms"] = round(self._tail[0].elapsed_time(self._tail[1]), 4)
+        self._events, self._tail = [], None
+        return out
 
     # -- protocol invariants ------------------------------------------------
     def protocol_errors(self) -> List[str]:
