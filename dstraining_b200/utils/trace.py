@@ -91,6 +91,20 @@ class StepProfiler:
         self.prof = None
 
 
+def busy_time(spans) -> float:
+    """Length of the union of ``(start, end)`` intervals (overlapping kernels
+    on several streams count once)."""
+    spans = sorted(spans)
+    busy, cur_s, cur_e = 0.0, spans[0][0], spans[0][1]
+    for s0, e0 in spans[1:]:
+        if s0 > cur_e:
+            busy += cur_e - cur_s
+            cur_s, cur_e = s0, e0
+        else:
+            cur_e = max(cur_e, e0)
+    return busy + (cur_e - cur_s)
+
+
 def kernel_summary(prof, steps: int = 1) -> str:
     """Device time per kernel name over a recorded window: calls and
     microseconds per step, share of the summed kernel time, and the device
@@ -113,16 +127,8 @@ def kernel_summary(prof, steps: int = 1) -> str:
         spans.append((ev.time_range.start, ev.time_range.end))
     if not spans:
         return "no device activity recorded\n"
-    spans.sort()
-    busy, cur_s, cur_e = 0.0, spans[0][0], spans[0][1]
-    for s0, e0 in spans[1:]:
-        if s0 > cur_e:
-            busy += cur_e - cur_s
-            cur_s, cur_e = s0, e0
-        else:
-            cur_e = max(cur_e, e0)
-    busy += cur_e - cur_s
-    wall = spans[-1][1] - spans[0][0]
+    busy = busy_time(spans)
+    wall = max(e for _, e in spans) - min(s for s, _ in spans)
     total = sum(v[1] for v in rows.values())
     out = [f"window: {steps} step(s); span {wall / steps:.1f} us/step; device busy {busy / steps:.1f} us/step "
            f"({busy / wall:.1%} of the span); summed kernel time {total / steps:.1f} us/step",

@@ -138,3 +138,11 @@ def test_fused_dp_adam_weight_decay_is_adamw():
         ref_opt.step()
     for (n, p), q in zip(m.named_parameters(), ref.parameters()):
         assert (p - q).abs().max().item() < 1e-5, n
+
+
+def test_device_busy_time_counts_overlaps_once():
+    from dstraining_b200.utils.trace import busy_time
+
+    # two streams overlapping on [2, 3), a gap [5, 6), a span nested in another
+    assert busy_time([(0.0, 3.0), (2.0, 5.0), (6.0, 10.0), (7.0, 8.0)]) == 9.0
+    assert busy_time([(1.0, 2.0)]) == 1.0
