@@ -3,6 +3,7 @@
     python -m dstraining_b200.utils.kernel_bench --suite gpt2        # every GPT-2-small shape
     python -m dstraining_b200.utils.kernel_bench --op gemm --m 16384 --n 3072 --k 768 --layout nt --epi bias_gelu
     python -m dstraining_b200.utils.kernel_bench --op attn --b 16 --t 1024 --h 12 --d 64 --dir bwd
+    python -m dstraining_b200.utils.kernel_bench --op tp_gather --tp 4   # fused TP GEMM, emulated on 1 GPU
 
 Each measurement: ``--warmup`` untimed calls, then ``--iters`` calls each
 timed alone with CUDA events on the launching stream, with a 256 MB buffer
@@ -106,6 +107,53 @@ def bench_attn(t, b, tl, h, d, direction, warmup, iters, mode=0):
     return ms, flops / (ms * 1e-3) / 1e12
 
 
+def bench_tp_local(t, kind, tp, tokens, hidden, ffn, seq, warmup, iters):
+    """The fused TP GEMMs run by ONE process on ONE GPU, with every "rank's"
+    buffer a local tensor and every peer flag already raised, so no launch
+    waits for another kernel: the kernel's own structure (copier warps, tile
+    order, arrival counters, receive slots, slot reduction) without NVLink,
+    small enough for ncu. ``kind``: ``gather`` (AG+GEMM: x[tokens/tp, hidden]
+    gathered, times W[ffn, hidden]^T) or ``scatter`` (GEMM+RS: h[tokens, ffn]
+    times W[hidden, ffn]^T, then the ordered slot reduction)."""
+    from dstraining_b200.ops import native
+    from dstraining_b200.ops.gemm import EPI_STORE
+
+    lib = native.lib()
+    rows = tokens // tp
+    flags = torch.full((64,), 1 << 30, dtype=torch.int32, device="cuda")  # every wait already satisfied
+    done = torch.zeros(2, dtype=torch.int32, device="cuda")
+    epoch = [0]
+    if kind == "gather":
+        shards = [bf(rows, hidden) for _ in range(tp)]
+        w = bf(ffn, hidden)
+        arrive = torch.zeros(-(-tokens // 128), dtype=torch.int32, device="cuda")
+        gath = torch.empty(tokens, hidden, dtype=torch.bfloat16, device="cuda")
+        ptrs = [x.data_ptr() for x in shards]
+
+        def fn():
+            epoch[0] += 1
+            lib.tp_gemm(shards[0], False, w, False, tokens, ffn, hidden, EPI_STORE, 1, ptrs, [flags.data_ptr()] * tp,
+                        done, 0, seq, epoch[0], gath=gath, arrive=arrive)
+
+        flops = 2.0 * tokens * ffn * hidden
+    else:
+        h = bf(tokens, ffn)
+        w = bf(hidden, ffn)
+        recv = [torch.empty(tp * rows, hidden, dtype=torch.bfloat16, device="cuda") for _ in range(tp)]
+        ptrs = [x.data_ptr() for x in recv]
+
+        def fn():
+            epoch[0] += 1
+            lib.tp_gemm(h, False, w, False, tokens, hidden, ffn, EPI_STORE, 3, ptrs, [flags.data_ptr()] * tp, done, 0,
+                        seq, epoch[0])
+            lib.tp_reduce(recv[0].view(tp, rows, hidden), tp, None, None, [flags.data_ptr()] * tp, done, 0, epoch[0])
+
+        flops = 2.0 * tokens * hidden * ffn
+    ms = t.run(fn, warmup, iters)
+    assert lib.read_status(True) == 0, "device status word set"
+    return ms, flops / (ms * 1e-3) / 1e12
+
+
 def bench_ln(t, rows, c, direction, warmup, iters):
     from dstraining_b200.ops import native
 
@@ -154,7 +202,12 @@ def gpt2_suite(t, warmup, iters):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--suite", choices=["gpt2"], default=None)
-    ap.add_argument("--op", choices=["gemm", "attn", "ln"], default="gemm")
+    ap.add_argument("--op", choices=["gemm", "attn", "ln", "tp_gather", "tp_scatter"], default="gemm")
+    ap.add_argument("--tp", type=int, default=4, help="tp_gather / tp_scatter: emulated group size")
+    ap.add_argument("--tokens", type=int, default=8192)
+    ap.add_argument("--hidden", type=int, default=2048)
+    ap.add_argument("--ffn", type=int, default=2048, help="per-rank FFN width")
+    ap.add_argument("--seq", type=int, default=2048)
     ap.add_argument("--m", type=int, default=16384)
     ap.add_argument("--n", type=int, default=3072)
     ap.add_argument("--k", type=int, default=768)
@@ -180,6 +233,9 @@ def main():
     elif a.op == "gemm":
         ms, tf = bench_gemm(t, a.m, a.n, a.k, a.layout, a.epi, a.warmup, a.iters)
         rows = [(f"gemm {a.layout} {a.epi}", f"{a.m}x{a.n}x{a.k}", ms, tf, "TFLOP/s")]
+    elif a.op in ("tp_gather", "tp_scatter"):
+        ms, tf = bench_tp_local(t, a.op[3:], a.tp, a.tokens, a.hidden, a.ffn, a.seq, a.warmup, a.iters)
+        rows = [(f"{a.op} (1 GPU, tp={a.tp})", f"{a.tokens}x{a.ffn}x{a.hidden}", ms, tf, "TFLOP/s")]
     elif a.op == "attn":
         ms, tf = bench_attn(t, a.b, a.t, a.h, a.d, a.dir, a.warmup, a.iters, a.attn_mode)
         rows = [(f"attention {a.dir}", f"b{a.b} t{a.t} h{a.h} d{a.d}", ms, tf, "TFLOP/s")]

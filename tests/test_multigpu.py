@@ -27,10 +27,13 @@ def _torchrun(n, script, *args, timeout=420):
     if torch.cuda.device_count() < n:
         pytest.skip(f"needs {n} GPUs")
     env = dict(os.environ, DST_PG_TIMEOUT_S="120", NCCL_NVLS_ENABLE="0")
-    cmd = ["timeout", "-k", "30", str(timeout), sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           f"--nproc-per-node={n}", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
-           os.path.join(ROOT, script), *args]
-    r = subprocess.run(cmd, env=env, cwd=ROOT, capture_output=True, text=True)
+    for _ in range(3):  # a port found free can be taken before the rendezvous binds it: pick another
+        cmd = ["timeout", "-k", "30", str(timeout), sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+               f"--nproc-per-node={n}", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
+               os.path.join(ROOT, script), *args]
+        r = subprocess.run(cmd, env=env, cwd=ROOT, capture_output=True, text=True)
+        if r.returncode == 0 or "EADDRINUSE" not in r.stderr:
+            break
     errors = [ln for ln in r.stderr.splitlines() if "error" in ln.lower() and not ln.startswith("frame #")]
     print(r.stdout[-4000:], "\n".join(errors[:20]), r.stderr[-2000:])
     assert r.returncode == 0
