@@ -204,7 +204,7 @@ def mlp(x, c_fc, c_proj, residual: Optional[torch.Tensor]):
     ):
         return tp_fused.mlp_sequence_parallel(x, c_fc.weight, c_fc.bias, c_proj.weight, c_proj.bias, residual, tp)
     if (
-        os.environ.get("DST_FUSED_TP_MLP", "0") == "1"  # not yet run on GPUs: off by default
+        os.environ.get("DST_FUSED_TP_MLP", "1") != "0"  # 0: NCCL all-reduces around the native GEMMs
         and c_fc.input_mode == "replicated"
         and c_proj.output_mode == "replicated"
         and x.dim() == 3

@@ -81,9 +81,6 @@ def plan(args) -> Dict:
         if seq % 128:
             warnings.append(f"sequence {seq} not a multiple of 128: "
                             + ("mma.sync attention kernels (slower)" if seq % 64 == 0 else "no native attention"))
-        if tp > 1 and not args.sp:
-            warnings.append("tensor parallelism without --sp: the MLP's all-reduces run on NCCL around the native "
-                            "GEMMs (DST_FUSED_TP_MLP=1 selects the fused form, not yet run on GPUs)")
         if tp > 1:
             if tp > 8:
                 warnings.append("more than 8 TP ranks: fused NVLink TP kernels unavailable (NCCL path)")

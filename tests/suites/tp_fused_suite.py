@@ -1,7 +1,7 @@
 """Fused tensor-parallel kernels (AG+GEMM, GEMM+RS over NVLink) vs tp=1.
 
     torchrun --nproc-per-node 2 tests/suites/tp_fused_suite.py --sp
-    torchrun --nproc-per-node 2 tests/suites/tp_fused_suite.py [--fused-mlp]
+    torchrun --nproc-per-node 2 tests/suites/tp_fused_suite.py [--nccl-mlp]
 
 bf16 on CUDA. Every rank builds the TP model and the single-GPU model with
 identical weights (decomposition-invariant init). Checks: the loss matches;
@@ -31,13 +31,14 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--sp", action="store_true")
     ap.add_argument("--device", default="cuda")
-    ap.add_argument("--fused-mlp", action="store_true",
-                    help="without --sp: the fused replicated-activation MLP (DST_FUSED_TP_MLP=1)")
+    ap.add_argument("--nccl-mlp", action="store_true",
+                    help="without --sp: the MLP with NCCL all-reduces around the native GEMMs (DST_FUSED_TP_MLP=0) "
+                    "instead of the fused replicated-activation form")
     a = ap.parse_args()
-    if a.fused_mlp:
+    if a.nccl_mlp:
         import os
 
-        os.environ["DST_FUSED_TP_MLP"] = "1"
+        os.environ["DST_FUSED_TP_MLP"] = "0"
     device = start(a.device)
     tp = topology.make_tp_context()
     rep = Report()

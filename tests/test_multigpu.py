@@ -61,11 +61,13 @@ def test_tp_fused_wide(n, sp):
     _torchrun(n, "tests/suites/tp_fused_suite.py", *(["--sp"] if sp else []))
 
 
-@pytest.mark.parametrize("n", [2, 4])
-def test_tp_fused_replicated_mlp(n):
-    """Plain TP (no SP): the MLP's all-reduces as scatter GEMM + slot reduction
-    + peer all-gather."""
-    _torchrun(n, "tests/suites/tp_fused_suite.py", "--fused-mlp")
+@pytest.mark.parametrize("n", [2])
+def test_tp_nccl_mlp_fallback(n):
+    """Plain TP (no SP) with the MLP's all-reduces on NCCL around the native
+    GEMMs (DST_FUSED_TP_MLP=0); the default, fused form (scatter GEMM + slot
+    reduction + peer all-gather) is what test_tp_fused_2gpu[False] and
+    test_tp_fused_wide[False-*] run."""
+    _torchrun(n, "tests/suites/tp_fused_suite.py", "--nccl-mlp")
 
 
 @pytest.mark.parametrize("n", [4, 8])

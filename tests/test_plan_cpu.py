@@ -52,7 +52,9 @@ def test_gpt2_preset():
     assert out["tokens_per_step"] == 16 * 1024
 
 
-def test_plain_tp_mlp_warning():
+def test_plain_tp_runs_fused_without_warning():
+    """Plain TP (no SP) keeps every TP collective on the fused NVLink kernels,
+    the MLP included, so the planner has nothing to warn about."""
     out = plan(parse_args(["--layers", "4", "--heads", "4", "--embd", "256", "--block", "256", "--vocab", "300",
                            "--tp", "2", "--bf16"]))
-    assert out["valid"] and any("without --sp" in w for w in out["fast_path_warnings"])
+    assert out["valid"] and not any("without --sp" in w for w in out["fast_path_warnings"])
