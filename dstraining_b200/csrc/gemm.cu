@@ -62,7 +62,7 @@ template <int BN, bool A_MN, bool B_MN, int EPI, int GATHER = 0, bool SCATTER = 
 static void launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const CUtensorMap& tx,
                        const GemmParams& p, int grid, cudaStream_t st, const PeerArgs* pa = nullptr) {
   auto kern = gemm_bf16_kernel<BN, A_MN, B_MN, EPI, GATHER, SCATTER>;
-  constexpr int smem = GemmCfg<BN>::kSmemBytes;
+  constexpr int smem = GemmCfg<BN, GATHER == 1 && !A_MN>::kSmemBytes;
   static bool configured[64] = {false};
   int dev;
   C10_CUDA_CHECK(cudaGetDevice(&dev));

@@ -168,17 +168,22 @@ constexpr int kGemmThreads = 224;  // producer, MMA, 4 epilogue warps, copier (g
 constexpr int kEpiChunk = 64;                        // columns per epilogue chunk
 constexpr int kStageTileBytes = 32 * kEpiChunk * 2;  // one 32x64 bf16 staging tile
 
-template <int BN>
+// RG: the row-gather (AG + GEMM) form, whose copier warp stages remote row
+// blocks through two 128 x 64 shared-memory tiles (one ring stage fewer).
+template <int BN, bool RG = false>
 struct GemmCfg {
   static constexpr int kStageA = kBM * kBK * 2;
   static constexpr int kStageB = BN * kBK * 2;
   static constexpr int kStageBytes = kStageA + kStageB;
-  static constexpr int kStages = (BN == 256) ? 4 : 6;
+  static constexpr int kStages = (BN == 256) ? (RG ? 3 : 4) : (RG ? 4 : 6);
   static constexpr int kTmemCols = 2 * BN;  // power of two: 256 or 512
   static constexpr int kOutStaging = 4 * 2 * kStageTileBytes;  // 4 warps x 2 tiles
   static constexpr int kBiasStaging = 4 * kEpiChunk * 4;       // 4 warps x 64 fp32
+  static constexpr int kCopyTile = kBM * 64 * 2;               // one 128-row x 64-column chunk
+  static constexpr int kCopyBytes = RG ? 1024 + 2 * kCopyTile : 0;  // aligned, double-buffered
   static constexpr int kSmemBytes =
-      kStages * kStageBytes + kOutStaging + kBiasStaging + 1024 /*align*/ + 256 /*barriers*/;
+      kStages * kStageBytes + kOutStaging + kBiasStaging + kCopyBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static_assert(kSmemBytes <= 232448, "GEMM: shared memory");
 };
 
 __device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float (&v)[32], int valid) {
@@ -224,9 +229,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmAux,
                      GemmParams p, const __grid_constant__ PeerArgs pa) {
-  using Cfg = GemmCfg<BN>;
-  constexpr int S = Cfg::kStages;
   constexpr bool kRowGather = (GATHER == 1 && !A_MN);  // rows of A gathered via the copier
+  using Cfg = GemmCfg<BN, kRowGather>;
+  constexpr int S = Cfg::kStages;
   static_assert(!(SCATTER && (EPI == kEpiPartialF32 || EPI == kEpiAccumF32 || EPI == kEpiBiasGelu ||
                               EPI == kEpiCEStats)),
                 "scatter mode takes a plain bf16 output");
@@ -237,12 +242,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* stage_base = smem;
   uint8_t* out_stage = smem + S * Cfg::kStageBytes;  // [4 warps][2][32x64 bf16], 1024-aligned
   float* bias_stage = reinterpret_cast<float*>(out_stage + Cfg::kOutStaging);  // [4 warps][64]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(out_stage + Cfg::kOutStaging + Cfg::kBiasStaging);
+  // row gather: two 1024-aligned copy tiles after the bias staging
+  uint8_t* copy_base = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(out_stage + Cfg::kOutStaging + Cfg::kBiasStaging) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(out_stage + Cfg::kOutStaging + Cfg::kBiasStaging + Cfg::kCopyBytes);
   uint64_t* full_bar = bars;               // [S]
   uint64_t* empty_bar = bars + S;          // [S]
   uint64_t* tfull_bar = bars + 2 * S;      // [2]
   uint64_t* tempty_bar = bars + 2 * S + 2; // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 4);
+  uint64_t* copy_bar = bars + 2 * S + 5;   // [2] (row gather)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -261,6 +270,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull_bar[i], 1);
       mbar_init(&tempty_bar[i], 128);
+      if (kRowGather) mbar_init(&copy_bar[i], 1);
     }
     fence_barrier_init();
   }
@@ -434,51 +444,80 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp >= 6) {
     // ------------------------------------------------------------ copier
     // Gather mode: pull every remote row block of A into the local gather
-    // buffer once, source by source in processing order; each copier warp
-    // claims the next 64-column chunk from a launch-wide counter, so the
-    // copies progress with whichever CTAs are resident (the kernel never
+    // buffer once, in processing order (the copier threads of all CTAs claim
+    // the next 128-row x 64-column chunk from a launch-wide counter, so the
+    // copies progress with whichever CTAs are resident: the kernel never
     // needs all of its CTAs on the GPU at once, e.g. next to NCCL kernels
     // that occupy some SMs). Each landed chunk bumps its block's counter.
-    if (kRowGather) {
+    if (kRowGather && elect_one()) {
+      // One thread drives bulk tensor copies through two shared-memory tiles:
+      // while chunk i is loaded (a plain TMA load from the owner's shard, no
+      // multicast), chunk i-1 is stored into the local gather buffer; a
+      // chunk's arrival is counted once its store has completed.
       const int per_src = num_m / pa.tp;
       const int total = (pa.tp - 1) * per_src * pa.kchunks;
       uint32_t ready = 0;
-      for (;;) {
-        int c = 0;
-        if (lane == 0) c = static_cast<int>(atomicAdd(pa.claim, 1u));
-        c = __shfl_sync(0xffffffff, c, 0);
-        if (c >= total) break;
-        const int mb = gather_mblock(pa, per_src + c / pa.kchunks, num_m);  // skip own blocks
-        const int kc = c % pa.kchunks;
-        int src, local;
-        token_owner(pa, mb * kBM, src, local);
-        if (!(ready & (1u << src))) {
-          int okr = 1;
-          if (lane == 0)
-            okr = flag_wait_geq(pa.flags[pa.rank] + kGReady * kMaxPeers + src, pa.epoch, p.status, kTimeoutPeer);
-          if (!__shfl_sync(0xffffffff, okr, 0)) break;
-          ready |= 1u << src;
-        }
-        const __nv_bfloat16* s = pa.shard[src] + static_cast<size_t>(local) * pa.shard_ld + kc * 64;
-        __nv_bfloat16* d = pa.gath + static_cast<size_t>(mb) * kBM * pa.shard_ld + kc * 64;
-#pragma unroll 1
-        for (int base = 0; base < kBM * 8; base += 32 * 16) {  // 16 loads in flight per lane
-          uint4 t[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int v = base + j * 32 + lane;
-            t[j] = *reinterpret_cast<const uint4*>(s + static_cast<size_t>(v >> 3) * pa.shard_ld + (v & 7) * 8);
+      uint32_t phase[2] = {0u, 0u};
+      int ld_mb = -1, ld_kc = 0;  // chunk whose load was issued last iteration (tile (i-1) & 1)
+      int st_mb = -1;             // chunk whose store was committed last iteration
+      bool ok = true, claiming = true;
+      for (int i = 0;; ++i) {
+        const int buf = i & 1;
+        // A: claim the next chunk and load it into tile `buf`
+        int new_mb = -1, new_kc = 0;
+        if (claiming && ok) {
+          const int c = static_cast<int>(atomicAdd(pa.claim, 1u));
+          if (c < total) {
+            new_mb = gather_mblock(pa, per_src + c / pa.kchunks, num_m);  // skip own blocks
+            new_kc = c % pa.kchunks;
+            int src, local;
+            token_owner(pa, new_mb * kBM, src, local);
+            if (!(ready & (1u << src))) {
+              if (flag_wait_geq(pa.flags[pa.rank] + kGReady * kMaxPeers + src, pa.epoch, p.status, kTimeoutPeer))
+                ready |= 1u << src;
+              else
+                ok = false;
+            }
+            if (ok) {
+              bulk_wait_read<0>();  // the store that last used this tile (committed last iteration) has read it
+              mbar_arrive_expect_tx(&copy_bar[buf], Cfg::kCopyTile);
+              tma_load_2d(copy_base + buf * Cfg::kCopyTile, &pa.gather[src], &copy_bar[buf], new_kc * 64, local);
+            } else {
+              new_mb = -1;
+            }
+          } else {
+            claiming = false;
           }
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int v = base + j * 32 + lane;
-            *reinterpret_cast<uint4*>(d + static_cast<size_t>(v >> 3) * pa.shard_ld + (v & 7) * 8) = t[j];
+        }
+        // B: the previous chunk's load has landed: store it into the gather buffer
+        bool committed = false;
+        if (ld_mb >= 0) {
+          const int pb = buf ^ 1;
+          if (mbar_wait(&copy_bar[pb], phase[pb], p.status, kTimeoutTmaFull)) {
+            phase[pb] ^= 1u;
+            tma_store_2d(&pa.gath_map, copy_base + pb * Cfg::kCopyTile, ld_kc * 64, ld_mb * kBM);
+            bulk_commit();
+            committed = true;
+          } else {
+            ok = false;
           }
         }
-        __threadfence();
-        __syncwarp();
-        if (lane == 0) atomicAdd(pa.arrive + mb, 1u);
+        // C: the store committed last iteration has completed: count its chunk
+        if (st_mb >= 0) {
+          if (committed)
+            bulk_wait_group<1>();
+          else
+            bulk_wait_group<0>();
+          fence_proxy_async_global();
+          __threadfence();
+          atomicAdd(pa.arrive + st_mb, 1u);
+        }
+        st_mb = committed ? ld_mb : -1;
+        ld_mb = new_mb;
+        ld_kc = new_kc;
+        if (ld_mb < 0 && st_mb < 0) break;  // nothing claimed, loading or storing
       }
+      bulk_wait_group<0>();
     }
   } else {
     // ------------------------------------------------------------ epilogue

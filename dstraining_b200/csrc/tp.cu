@@ -46,46 +46,68 @@ __global__ void __launch_bounds__(256) reduce_kernel(const __grid_constant__ Red
     const int vpr = a.N / 8;
     const int64_t total = static_cast<int64_t>(a.rows) * vpr;
     const size_t slot = static_cast<size_t>(a.rows) * a.N;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-      const int row = static_cast<int>(i / vpr), c8 = static_cast<int>(i % vpr) * 8;
-      const size_t off = static_cast<size_t>(row) * a.N + c8;
-      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      for (int s = 0; s < a.tp; ++s) {  // fixed rank order
-        const uint4 u = *reinterpret_cast<const uint4*>(a.recv + s * slot + off);
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    // two 8-element vectors per thread and iteration, every slot's loads of
+    // both issued before any is summed
+    for (int64_t i0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i0 < total; i0 += 2 * stride) {
+      constexpr int V = 2;
+      int64_t iv[V];
+      bool in[V];
+      uint4 u[V][kMaxPeers];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 f = __bfloat1622float2(h[j]);
-          acc[2 * j] += f.x;
-          acc[2 * j + 1] += f.y;
-        }
+      for (int v = 0; v < V; ++v) {
+        iv[v] = i0 + v * stride;
+        in[v] = iv[v] < total;
+        const int row = static_cast<int>(iv[v] / vpr), c8 = static_cast<int>(iv[v] % vpr) * 8;
+        const size_t off = static_cast<size_t>(row) * a.N + c8;
+#pragma unroll
+        for (int s = 0; s < kMaxPeers; ++s)
+          if (in[v] && s < a.tp) u[v][s] = *reinterpret_cast<const uint4*>(a.recv + s * slot + off);
       }
-      if (a.bias) {
-        const uint4 u = *reinterpret_cast<const uint4*>(a.bias + c8);
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 f = __bfloat1622float2(h[j]);
-          acc[2 * j] += f.x;
-          acc[2 * j + 1] += f.y;
+      for (int v = 0; v < V; ++v) {
+        if (!in[v]) continue;
+        const int row = static_cast<int>(iv[v] / vpr), c8 = static_cast<int>(iv[v] % vpr) * 8;
+        const size_t off = static_cast<size_t>(row) * a.N + c8;
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+        for (int s = 0; s < kMaxPeers; ++s) {  // summed in fixed rank order
+          if (s < a.tp) {
+            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u[v][s]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 f = __bfloat1622float2(h[j]);
+              acc[2 * j] += f.x;
+              acc[2 * j + 1] += f.y;
+            }
+          }
         }
-      }
-      if (a.resid) {
-        const uint4 u = *reinterpret_cast<const uint4*>(a.resid + off);
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+        if (a.bias) {
+          const uint4 bu = *reinterpret_cast<const uint4*>(a.bias + c8);
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&bu);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 f = __bfloat1622float2(h[j]);
-          acc[2 * j] += f.x;
-          acc[2 * j + 1] += f.y;
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = __bfloat1622float2(h[j]);
+            acc[2 * j] += f.x;
+            acc[2 * j + 1] += f.y;
+          }
         }
-      }
-      uint4 o;
-      __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+        if (a.resid) {
+          const uint4 ru = *reinterpret_cast<const uint4*>(a.resid + off);
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&ru);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) oh[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
-      *reinterpret_cast<uint4*>(a.out + off) = o;
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = __bfloat1622float2(h[j]);
+            acc[2 * j] += f.x;
+            acc[2 * j + 1] += f.y;
+          }
+        }
+        uint4 o;
+        __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) oh[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
+        *reinterpret_cast<uint4*>(a.out + off) = o;
+      }
     }
   }
   __syncthreads();
@@ -184,7 +206,11 @@ at::Tensor tp_reduce(const at::Tensor& recv, int64_t tp_size, const c10::optiona
   a.N = N;
   a.epoch = static_cast<uint32_t>(epoch);
   a.status = status_ptr();
-  tp::reduce_kernel<<<grid_for(static_cast<int64_t>(rows) * N / 8), 256, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  // about two CTAs per SM: enough loads in flight (2 vectors x tp slots per thread) without a long
+  // tail of CTAs with almost no work behind the launch-wide completion counter
+  const int64_t vecs = static_cast<int64_t>(rows) * N / 8;
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((vecs + 511) / 512, 2 * num_sms())));
+  tp::reduce_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return out;
 }

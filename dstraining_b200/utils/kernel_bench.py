@@ -108,50 +108,38 @@ def bench_attn(t, b, tl, h, d, direction, warmup, iters, mode=0):
 
 
 def bench_tp_local(t, kind, tp, tokens, hidden, ffn, seq, warmup, iters):
-    """The fused TP GEMMs run by ONE process on ONE GPU, with every "rank's"
-    buffer a local tensor and every peer flag already raised, so no launch
-    waits for another kernel: the kernel's own structure (copier warps, tile
-    order, arrival counters, receive slots, slot reduction) without NVLink,
-    small enough for ncu. ``kind``: ``gather`` (AG+GEMM: x[tokens/tp, hidden]
-    gathered, times W[ffn, hidden]^T) or ``scatter`` (GEMM+RS: h[tokens, ffn]
-    times W[hidden, ffn]^T, then the ordered slot reduction)."""
+    """The fused TP GEMMs as rank 0 of an emulated group on ONE GPU (every
+    "rank's" buffer local, every peer flag raised: no launch waits for
+    another kernel; see utils/tp_emulate.py): the kernel's own structure
+    without NVLink, small enough for ncu. ``kind``: ``gather`` (AG+GEMM) or
+    ``scatter`` (GEMM+RS with the ordered slot reduction)."""
     from dstraining_b200.ops import native
-    from dstraining_b200.ops.gemm import EPI_STORE
+    from dstraining_b200.utils.tp_emulate import GatherEmulation, ScatterEmulation
 
-    lib = native.lib()
-    rows = tokens // tp
-    flags = torch.full((64,), 1 << 30, dtype=torch.int32, device="cuda")  # every wait already satisfied
-    done = torch.zeros(2, dtype=torch.int32, device="cuda")
-    epoch = [0]
-    if kind == "gather":
-        shards = [bf(rows, hidden) for _ in range(tp)]
-        w = bf(ffn, hidden)
-        arrive = torch.zeros(-(-tokens // 128), dtype=torch.int32, device="cuda")
-        gath = torch.empty(tokens, hidden, dtype=torch.bfloat16, device="cuda")
-        ptrs = [x.data_ptr() for x in shards]
-
-        def fn():
-            epoch[0] += 1
-            lib.tp_gemm(shards[0], False, w, False, tokens, ffn, hidden, EPI_STORE, 1, ptrs, [flags.data_ptr()] * tp,
-                        done, 0, seq, epoch[0], gath=gath, arrive=arrive)
-
-        flops = 2.0 * tokens * ffn * hidden
-    else:
-        h = bf(tokens, ffn)
-        w = bf(hidden, ffn)
-        recv = [torch.empty(tp * rows, hidden, dtype=torch.bfloat16, device="cuda") for _ in range(tp)]
-        ptrs = [x.data_ptr() for x in recv]
-
-        def fn():
-            epoch[0] += 1
-            lib.tp_gemm(h, False, w, False, tokens, hidden, ffn, EPI_STORE, 3, ptrs, [flags.data_ptr()] * tp, done, 0,
-                        seq, epoch[0])
-            lib.tp_reduce(recv[0].view(tp, rows, hidden), tp, None, None, [flags.data_ptr()] * tp, done, 0, epoch[0])
-
-        flops = 2.0 * tokens * hidden * ffn
-    ms = t.run(fn, warmup, iters)
-    assert lib.read_status(True) == 0, "device status word set"
-    return ms, flops / (ms * 1e-3) / 1e12
+    em = (GatherEmulation if kind == "gather" else ScatterEmulation)(tp, tokens, hidden, ffn, seq)
+    ms = t.run(em.run, warmup, iters)
+    if kind == "gather" and os.environ.get("DST_BENCH_PRECOPIED"):
+        # the GEMM part alone: blocks already copied (the set-up copies are timed too, so report the
+        # kernel from a separate event pair)
+        times = []
+        for _ in range(iters):
+            em.run(precopied=True)  # warm
+            torch.cuda.synchronize()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            em.gath.copy_(em.gathered())
+            em.epoch += 1
+            em.arrive.fill_(em.epoch * (hidden // 64))
+            em.done[1] = (tp - 1) * ((tokens // 128) // tp) * (hidden // 64)
+            em.epoch -= 1
+            t.flush.fill_(1.0)
+            s.record()
+            em.run()
+            e.record()
+            torch.cuda.synchronize()
+            times.append(s.elapsed_time(e))
+        print(f"precopied gather GEMM: {sum(times) / len(times):.4f} ms")
+    assert native.lib().read_status(True) == 0, "device status word set"
+    return ms, 2.0 * tokens * ffn * hidden / (ms * 1e-3) / 1e12
 
 
 def bench_ln(t, rows, c, direction, warmup, iters):

@@ -367,3 +367,41 @@ def test_flash_backward_tcgen05(B, T, H, D, mode):
         assert _rel(gv[..., i, :], go[..., i, :]) < 3e-2, name
     assert torch.equal(g, lib.flash_attn_bwd_tc(dout, qkv, out, lse, H, D, mode))
     assert lib.read_status(True) == 0
+
+
+@pytest.mark.parametrize("tp", [2, 4, 8])
+def test_tp_gather_gemm_emulated(tp):
+    """The AG+GEMM kernel as rank 0 of a group of ``tp`` with every rank's
+    shard local (no cross-kernel waits): remote row blocks copied through
+    the copier's shared-memory tiles, own rows read in place; equal to the
+    plain GEMM of the gathered input, twice in a row (the arrival counters
+    and claim counter carry over between launches)."""
+    from dstraining_b200.ops.gemm import gemm
+    from dstraining_b200.utils.tp_emulate import GatherEmulation
+
+    lib = _lib()
+    em = GatherEmulation(tp, tokens=2 * 128 * tp * 2, hidden=256, ffn=384, seq=128 * tp * 2, seed=tp)
+    ref = gemm(em.gathered(), False, em.w, False)
+    for _ in range(2):
+        out = em.run()
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref)
+    assert lib.read_status(True) == 0
+
+
+@pytest.mark.parametrize("tp", [2, 4, 8])
+def test_tp_scatter_gemm_emulated(tp):
+    """The GEMM+RS kernel and slot reduction as rank 0 of a group of ``tp``
+    (other ranks' slots zero): rank 0's rows of the plain product, twice."""
+    from dstraining_b200.ops.gemm import gemm
+    from dstraining_b200.utils.tp_emulate import ScatterEmulation
+
+    lib = _lib()
+    em = ScatterEmulation(tp, tokens=2 * 128 * tp * 2, hidden=256, ffn=384, seq=128 * tp * 2, seed=tp)
+    full = gemm(em.h, False, em.w, False)
+    ref = full[em.own_rows()]
+    for _ in range(2):
+        out = em.run()
+        torch.cuda.synchronize()
+        assert _rel(out, ref) < 1e-2
+    assert lib.read_status(True) == 0
