@@ -107,7 +107,7 @@ def bench_attn(t, b, tl, h, d, direction, warmup, iters, mode=0):
     return ms, flops / (ms * 1e-3) / 1e12
 
 
-def bench_tp_local(t, kind, tp, tokens, hidden, ffn, seq, warmup, iters):
+def bench_tp_local(t, kind, tp, tokens, hidden, ffn, seq, warmup, iters, precopied=False):
     """The fused TP GEMMs as rank 0 of an emulated group on ONE GPU (every
     "rank's" buffer local, every peer flag raised: no launch waits for
     another kernel; see utils/tp_emulate.py): the kernel's own structure
@@ -118,7 +118,7 @@ def bench_tp_local(t, kind, tp, tokens, hidden, ffn, seq, warmup, iters):
 
     em = (GatherEmulation if kind == "gather" else ScatterEmulation)(tp, tokens, hidden, ffn, seq)
     ms = t.run(em.run, warmup, iters)
-    if kind == "gather" and os.environ.get("DST_BENCH_PRECOPIED"):
+    if kind == "gather" and precopied:
         # the GEMM part alone: blocks already copied (the set-up copies are timed too, so report the
         # kernel from a separate event pair)
         times = []
@@ -196,6 +196,8 @@ def main():
     ap.add_argument("--hidden", type=int, default=2048)
     ap.add_argument("--ffn", type=int, default=2048, help="per-rank FFN width")
     ap.add_argument("--seq", type=int, default=2048)
+    ap.add_argument("--precopied", action="store_true",
+                    help="tp_gather: also time the GEMM part alone (remote blocks copied beforehand)")
     ap.add_argument("--m", type=int, default=16384)
     ap.add_argument("--n", type=int, default=3072)
     ap.add_argument("--k", type=int, default=768)
@@ -222,7 +224,8 @@ def main():
         ms, tf = bench_gemm(t, a.m, a.n, a.k, a.layout, a.epi, a.warmup, a.iters)
         rows = [(f"gemm {a.layout} {a.epi}", f"{a.m}x{a.n}x{a.k}", ms, tf, "TFLOP/s")]
     elif a.op in ("tp_gather", "tp_scatter"):
-        ms, tf = bench_tp_local(t, a.op[3:], a.tp, a.tokens, a.hidden, a.ffn, a.seq, a.warmup, a.iters)
+        ms, tf = bench_tp_local(t, a.op[3:], a.tp, a.tokens, a.hidden, a.ffn, a.seq, a.warmup, a.iters,
+                                a.precopied)
         rows = [(f"{a.op} (1 GPU, tp={a.tp})", f"{a.tokens}x{a.ffn}x{a.hidden}", ms, tf, "TFLOP/s")]
     elif a.op == "attn":
         ms, tf = bench_attn(t, a.b, a.t, a.h, a.d, a.dir, a.warmup, a.iters, a.attn_mode)
