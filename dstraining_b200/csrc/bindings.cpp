@@ -42,7 +42,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_embed(m);
   register_adam(m);
   register_ce(m);
-  register_attn(m);
   register_attn_tc(m);
   register_symm(m);
   register_tp(m);

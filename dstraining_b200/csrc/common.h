@@ -25,7 +25,6 @@ void register_norm(pybind11::module& m);
 void register_embed(pybind11::module& m);
 void register_adam(pybind11::module& m);
 void register_ce(pybind11::module& m);
-void register_attn(pybind11::module& m);
 void register_attn_tc(pybind11::module& m);
 void register_symm(pybind11::module& m);
 void register_tp(pybind11::module& m);

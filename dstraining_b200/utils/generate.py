@@ -18,9 +18,9 @@ probability ``top_p``.
   exactly as without a cache. Runs on the model's own parameters with
   PyTorch ops (fp32 on CPU, the model's dtype on CUDA).
 * Otherwise every step runs the model's full-context forward pass on the
-  last ``block_size`` tokens, right-padded to a multiple of ``pad_to`` so the
-  native causal attention kernels (which
-  take sequence lengths in multiples of 64 / 128) can run it - under causal
+  last ``block_size`` tokens, right-padded to a multiple of ``pad_to`` (the
+  native causal attention kernels' 128-row tiles, so the sequence-parallel
+  and fused tensor-parallel layers see whole tiles too) - under causal
   attention the padding never influences the positions before it. Every TP
   rank must call it with the same inputs and generator state; pipeline
   stages are not supported.

@@ -86,22 +86,22 @@ def bench_gemm(t, m, n, k, layout, epi, warmup, iters):
 def bench_attn(t, b, tl, h, d, direction, warmup, iters, mode=0):
     from dstraining_b200.ops import native
 
+    from dstraining_b200.ops.flash import padded_length
+
     lib = native.lib()
+    if tl % 128:  # the model zero-pads such lengths up to the kernels' 128-row tiles
+        tl = padded_length(tl)
     qkv = bf(b, tl, 3 * h * d)
-    if tl % 128 == 0:  # the model's dispatch (mode 0); 1 / 2 force the ping-pong / one-tile forward
-        fwd = lambda q, hh, dd: lib.flash_attn_fwd_tc(q, hh, dd, mode)  # noqa: E731
-    else:
-        fwd = lib.flash_attn_fwd
+    # mode 0: the model's dispatch; 1 / 2 force the ping-pong / one-tile forward
+    fwd = lambda q, hh, dd: lib.flash_attn_fwd_tc(q, hh, dd, mode)  # noqa: E731
     out, lse = fwd(qkv, h, d)
     dout = bf(b, tl, h * d)
     if direction == "fwd":
         fn = lambda: fwd(qkv, h, d)  # noqa: E731
         flops = 4.0 * b * h * tl * tl * d / 2
     else:
-        if tl % 128 == 0:  # mode 0: double-buffered kernels; 2: single-buffered
-            fn = lambda: lib.flash_attn_bwd_tc(dout, qkv, out, lse, h, d, mode)  # noqa: E731
-        else:
-            fn = lambda: lib.flash_attn_bwd(dout, qkv, out, lse, h, d)  # noqa: E731
+        # mode 0: double-buffered kernels; 2: single-buffered
+        fn = lambda: lib.flash_attn_bwd_tc(dout, qkv, out, lse, h, d, mode)  # noqa: E731
         flops = 10.0 * b * h * tl * tl * d / 2  # dV, dK, dQ, dP + the recomputed S
     ms = t.run(fn, warmup, iters)
     return ms, flops / (ms * 1e-3) / 1e12

@@ -9,8 +9,8 @@ Takes ``train.py``'s flags and reports, without building the model:
   schedules enforce: heads and d_ff by tp, layers by pp x chunks,
   micro-batches by pp for interleaving, sequence by tp under SP);
 * whether it stays on the fast native paths on CUDA with ``--bf16``: the
-  tcgen05 attention kernels need a sequence length that is a multiple of 128
-  (64 falls back to the mma.sync kernels), head size 64 or 128; the fused
+  tcgen05 attention kernels take head size 64 or 128 and run on 128-row
+  tiles (other sequence lengths are zero-padded up to one); the fused
   NVLink tensor-parallel kernels need sequence shards of a multiple of 128
   tokens and at most 8 TP ranks; the one-kernel NVLink DP optimizer needs at
   most 8 replicas on one machine (otherwise its NCCL form runs);
@@ -79,8 +79,8 @@ def plan(args) -> Dict:
         if head_dim not in (64, 128):
             warnings.append(f"head size {head_dim}: native attention takes 64 or 128")
         if seq % 128:
-            warnings.append(f"sequence {seq} not a multiple of 128: "
-                            + ("mma.sync attention kernels (slower)" if seq % 64 == 0 else "no native attention"))
+            warnings.append(f"sequence {seq} not a multiple of 128: attention zero-pads it to "
+                            f"{-(-seq // 128) * 128} (padded rows computed and discarded)")
         if tp > 1:
             if tp > 8:
                 warnings.append("more than 8 TP ranks: fused NVLink TP kernels unavailable (NCCL path)")

@@ -3,6 +3,8 @@ of the same op (inputs rounded to bf16 first, so only the kernel's own
 arithmetic is measured). Small and ragged shapes exercise the bounds paths.
 """
 
+import math
+
 import pytest
 import torch
 import torch.nn.functional as F
@@ -168,7 +170,20 @@ def _ref_attention(qkv, H, D):
     return o.transpose(1, 2).reshape(B, T, H * D)
 
 
-@pytest.mark.parametrize("B,T,H,D", [(2, 128, 4, 64), (2, 256, 2, 128), (1, 1024, 12, 64), (1, 2048, 2, 128)])
+def _ref_lse2(qkv, H, D):
+    """Base-2 log-sum-exp of the causal scaled scores, [B, H, T] (what the
+    forward kernels save for backward)."""
+    B, T, _ = qkv.shape
+    y = qkv.float().view(B, T, H, 3, D)
+    q, k = y[:, :, :, 0].transpose(1, 2), y[:, :, :, 1].transpose(1, 2)
+    s = (q @ k.transpose(-2, -1)) / D**0.5
+    s = s.masked_fill(torch.ones(T, T, dtype=torch.bool, device=s.device).triu(1), float("-inf"))
+    return torch.logsumexp(s, -1) / math.log(2.0)
+
+
+# T = 200 and 300: not multiples of the kernels' 128-row tiles, zero-padded by ops/flash.py
+@pytest.mark.parametrize("B,T,H,D", [(2, 128, 4, 64), (2, 256, 2, 128), (1, 1024, 12, 64), (1, 2048, 2, 128),
+                                     (2, 200, 4, 64), (1, 300, 2, 128)])
 def test_flash_attention(B, T, H, D):
     from dstraining_b200.ops.flash import flash_attention
 
@@ -256,16 +271,14 @@ def test_adamw_matches_torch():
 
 @pytest.mark.parametrize("B,T,H,D", [(2, 128, 4, 64), (1, 512, 3, 128), (2, 1024, 12, 64), (1, 2048, 2, 128)])
 def test_flash_forward_tcgen05(B, T, H, D):
-    """The tcgen05 forward matches the fp32 reference and the mma.sync
-    forward, including the saved log-sum-exp that backward consumes."""
+    """The tcgen05 forward matches the fp32 reference, including the saved
+    base-2 log-sum-exp that backward consumes."""
     lib = _lib()
     qkv = _bf(B, T, 3 * H * D, seed=30)
     out, lse = lib.flash_attn_fwd_tc(qkv, H, D)
     ref = _ref_attention(qkv, H, D)
     assert _rel(out, ref) < 2e-2
-    out2, lse2 = lib.flash_attn_fwd(qkv, H, D)
-    assert (lse - lse2).abs().max().item() < 2e-2
-    assert _rel(out, out2) < 2e-2
+    assert (lse - _ref_lse2(qkv, H, D)).abs().max().item() < 2e-2
 
 
 @pytest.mark.parametrize("B,T,H,D", [(2, 256, 4, 64), (1, 1024, 3, 128), (2, 1024, 12, 64), (1, 2048, 2, 128)])
@@ -294,20 +307,17 @@ def test_flash_forward_pingpong(B, T, H, D, growing):
 @pytest.mark.parametrize("mode", [0, 2])
 def test_flash_backward_tcgen05(B, T, H, D, mode):
     """tcgen05 backward (double-buffered kernels: mode 0; single-buffered:
-    mode 2) vs the fp32 reference and the mma.sync backward; bitwise
-    deterministic across runs."""
+    mode 2) vs the fp32 reference; bitwise deterministic across runs."""
     lib = _lib()
     qkv = _bf(B, T, 3 * H * D, seed=40)
     dout = _bf(B, T, H * D, seed=41)
     out, lse = lib.flash_attn_fwd_tc(qkv, H, D)
     g = lib.flash_attn_bwd_tc(dout, qkv, out, lse, H, D, mode)
-    g_old = lib.flash_attn_bwd(dout, qkv, out, lse, H, D)
     qr = qkv.float().requires_grad_(True)
     _ref_attention(qr, H, D).backward(dout.float())
-    gv, gr, go = g.float().view(B, T, H, 3, D), qr.grad.view(B, T, H, 3, D), g_old.float().view(B, T, H, 3, D)
+    gv, gr = g.float().view(B, T, H, 3, D), qr.grad.view(B, T, H, 3, D)
     for i, name in enumerate("qkv"):
         assert _rel(gv[..., i, :], gr[..., i, :]) < 3e-2, name
-        assert _rel(gv[..., i, :], go[..., i, :]) < 3e-2, name
     assert torch.equal(g, lib.flash_attn_bwd_tc(dout, qkv, out, lse, H, D, mode))
     assert lib.read_status(True) == 0
 

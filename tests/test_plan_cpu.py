@@ -33,7 +33,7 @@ def test_reports_invalid_and_slow_layouts(capsys):
     slow = plan(parse_args(["--layers", "4", "--heads", "4", "--embd", "256", "--block", "192", "--vocab", "300",
                             "--tp", "2", "--sp", "--bf16"]))
     assert slow["valid"] and any("fused TP" in w for w in slow["fast_path_warnings"])
-    assert any("mma.sync" in w for w in slow["fast_path_warnings"])
+    assert any("zero-pads it to 256" in w for w in slow["fast_path_warnings"])
     good = plan(parse_args(["--layers", "24", "--heads", "16", "--embd", "2048", "--block", "2048", "--vocab",
                             "50304", "--tp", "2", "--pp", "2", "--dp", "2", "--sp", "--bf16", "--vp", "--batch", "32",
                             "--micro", "2"]))
