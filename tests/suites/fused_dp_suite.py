@@ -27,6 +27,11 @@ from dstraining_b200.parallel import topology
 from dstraining_b200.parallel.dp import GradReducer
 
 
+# |g| at or below this fraction of the largest |g| of the same parameter and
+# step is within a few hundred ulps of fp32 summation noise for these sizes.
+NOISE_FLOOR = 1e-5
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--dp", type=int, default=2)
@@ -63,6 +68,7 @@ def main():
         ref = GPT(cfg, topology.SINGLE, seed=SEED).to(device)
         ref_opt = torch.optim.Adam(ref.parameters(), lr=1e-3)
     worst_loss = 0.0
+    noisy = {}  # fp32: reference elements whose gradient ever sat at the rounding-noise level
     for s in range(steps):
         idx, tgt = batch(cfg, B, SEED + 10 + s, device)
         mine = slice(dp.rank * b, (dp.rank + 1) * b)
@@ -80,6 +86,11 @@ def main():
         else:
             _, rl = ref(idx, tgt)
             rl.backward()
+        if not a.bf16:
+            for n_, p_ in ref.named_parameters():
+                g_ = p_.grad.detach()
+                tiny = (g_ != 0) & (g_.abs() <= NOISE_FLOOR * g_.abs().max())
+                noisy[n_] = noisy[n_] | tiny if n_ in noisy else tiny
         ref_opt.step()
         lm = loss.detach().float().clone()
         dist.all_reduce(lm, group=dp.group)
@@ -89,17 +100,32 @@ def main():
             rlm /= dp.world
         worst_loss = max(worst_loss, abs(lm.item() / dp.world - rlm.item()))
     rep.close("loss trajectory vs reference", worst_loss, atol=2e-2 if a.bf16 else 1e-5)
-    worst = 0.0
+    worst, worst_noisy, n_noisy = 0.0, 0.0, 0
     ref_p = dict(ref.named_parameters())
     for name, p in model.named_parameters():
         r = ref_p[name].data
         if not a.bf16 and p.shape != r.shape:
             continue  # TP shard vs full reference: covered by the loss check
-        worst = max(worst, max_diff(p.data, r))
-    # Adam normalises each update, so summation-order noise in near-zero
-    # gradients shows up at ~lr * 1e-2 in the weights; the reference suites
-    # hold trajectories to 1e-4 for the same reason.
+        diff = (p.data.float() - r.float()).abs()
+        if not a.bf16:
+            # Adam divides each update by the gradient's own running magnitude,
+            # so an element whose gradient was once at the rounding-noise level
+            # (a different summation order may even flip its sign) moves by up
+            # to lr in either run: it is held only to that bound. Examples: the
+            # key part of the qkv bias, whose exact gradient is zero (softmax is
+            # unchanged when every key of a row shifts by the same q.b), and an
+            # embedding row whose token's contributions cancel.
+            mask = noisy[name]
+            n_noisy += int(mask.sum())
+            if mask.any():
+                worst_noisy = max(worst_noisy, diff[mask].max().item())
+            diff = diff[~mask]
+        if diff.numel():
+            worst = max(worst, diff.max().item())
     rep.close("final parameters vs reference", worst, atol=2e-2 if a.bf16 else 1e-4)
+    if not a.bf16:
+        rep.close(f"final parameters with a noise-level gradient ({n_noisy} elements) within steps x lr", worst_noisy,
+                  atol=steps * 1e-3)
     # replicas must hold bitwise-identical parameters
     flat = torch.cat([p.data.float().reshape(-1) for p in model.parameters()])
     parts = [torch.empty_like(flat) for _ in range(dp.world)]
