@@ -15,7 +15,7 @@ bf16 rounding, and parameters must stay identical across DP ranks.
 
 import argparse
 
-from common import SEED, Report, batch, max_diff, small_config, start
+from common import SEED, NoiseLevelGrads, Report, batch, max_diff, small_config, start
 
 import torch
 import torch.distributed as dist
@@ -25,11 +25,6 @@ from dstraining_b200.optim.fused_dp import FusedDPAdam
 from dstraining_b200.optim.precision import MasterWeightOptimizer
 from dstraining_b200.parallel import topology
 from dstraining_b200.parallel.dp import GradReducer
-
-
-# |g| at or below this fraction of the largest |g| of the same parameter and
-# step is within a few hundred ulps of fp32 summation noise for these sizes.
-NOISE_FLOOR = 1e-5
 
 
 def main():
@@ -68,7 +63,7 @@ def main():
         ref = GPT(cfg, topology.SINGLE, seed=SEED).to(device)
         ref_opt = torch.optim.Adam(ref.parameters(), lr=1e-3)
     worst_loss = 0.0
-    noisy = {}  # fp32: reference elements whose gradient ever sat at the rounding-noise level
+    noisy = NoiseLevelGrads()  # fp32: reference elements with a noise-level gradient
     for s in range(steps):
         idx, tgt = batch(cfg, B, SEED + 10 + s, device)
         mine = slice(dp.rank * b, (dp.rank + 1) * b)
@@ -87,10 +82,7 @@ def main():
             _, rl = ref(idx, tgt)
             rl.backward()
         if not a.bf16:
-            for n_, p_ in ref.named_parameters():
-                g_ = p_.grad.detach()
-                tiny = (g_ != 0) & (g_.abs() <= NOISE_FLOOR * g_.abs().max())
-                noisy[n_] = noisy[n_] | tiny if n_ in noisy else tiny
+            noisy.record(ref)
         ref_opt.step()
         lm = loss.detach().float().clone()
         dist.all_reduce(lm, group=dp.group)
@@ -100,28 +92,10 @@ def main():
             rlm /= dp.world
         worst_loss = max(worst_loss, abs(lm.item() / dp.world - rlm.item()))
     rep.close("loss trajectory vs reference", worst_loss, atol=2e-2 if a.bf16 else 1e-5)
-    worst, worst_noisy, n_noisy = 0.0, 0.0, 0
     ref_p = dict(ref.named_parameters())
-    for name, p in model.named_parameters():
-        r = ref_p[name].data
-        if not a.bf16 and p.shape != r.shape:
-            continue  # TP shard vs full reference: covered by the loss check
-        diff = (p.data.float() - r.float()).abs()
-        if not a.bf16:
-            # Adam divides each update by the gradient's own running magnitude,
-            # so an element whose gradient was once at the rounding-noise level
-            # (a different summation order may even flip its sign) moves by up
-            # to lr in either run: it is held only to that bound. Examples: the
-            # key part of the qkv bias, whose exact gradient is zero (softmax is
-            # unchanged when every key of a row shifts by the same q.b), and an
-            # embedding row whose token's contributions cancel.
-            mask = noisy[name]
-            n_noisy += int(mask.sum())
-            if mask.any():
-                worst_noisy = max(worst_noisy, diff[mask].max().item())
-            diff = diff[~mask]
-        if diff.numel():
-            worst = max(worst, diff.max().item())
+    pairs = [(name, p.data, ref_p[name].data) for name, p in model.named_parameters()
+             if a.bf16 or p.shape == ref_p[name].shape]  # TP shards vs full reference: covered by the loss check
+    worst, worst_noisy, n_noisy = noisy.compare(pairs)
     rep.close("final parameters vs reference", worst, atol=2e-2 if a.bf16 else 1e-4)
     if not a.bf16:
         rep.close(f"final parameters with a noise-level gradient ({n_noisy} elements) within steps x lr", worst_noisy,
